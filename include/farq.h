@@ -1,0 +1,151 @@
+/*
+ * farq.h — C ABI of the B200 (sm_100a) fused residual-add + RMSNorm +
+ * per-token group quantisation library (libfarq.so).
+ *
+ * The library replaces the device work behind the reference operator
+ *   fused_add_rmsnorm_group_quant(x, residual, gamma, residual_out, norm_out,
+ *                                 x_q, x_scale, eps, group_size)
+ * in src/task01_fused_add_rmsnorm_group_quant.py:1731-1851 of
+ * sinpeyw/flagos-kernelgen-72h-shanghai-2026, i.e. the Triton kernels it routes
+ * to on NVIDIA parts:
+ *   _preweighted_full_row_kernel                  (task01…py:65-121)
+ *   _preweighted_segmented_streaming_kernel       (task01…py:1127-1348)
+ *   _nvidia_parallel_row_group_streaming_kernel   (task01…py:1401-1546)
+ * All three compute the same per-row math; one kernel here covers all of them.
+ *
+ * Per row m (all arithmetic in fp32, d = 0..D-1, g = d / G):
+ *   r[d]     = f32(x[m,d]) + f32(residual[m,d])        -> residual_out (RNE)
+ *   inv_rms  = 1 / sqrt(sum_d r[d]^2 / D + eps)
+ *   w[d]     = r[d] * f32(gamma[d])
+ *   norm[d]  = w[d] * inv_rms                           -> norm_out (RNE, optional)
+ *   scale[g] = max(max_{d in g} |w[d]| * (inv_rms / QMAX), 1e-12)
+ *              (UE8M0 flag: rounded up to a power of two)
+ *   q[d]     = INT8 : trunc(clamp(norm[d] * (1/scale[g]), -127, 127)), QMAX = 127
+ *              E4M3 : rne_satfinite_e4m3(norm[d] * (1/scale[g])),       QMAX = 448
+ *
+ * Memory contract: destination passing. Every pointer is a device pointer the
+ * caller owns; nothing is allocated by farq_launch. The launch is asynchronous
+ * on the given stream and performs no host synchronisation. residual_out may
+ * alias x or residual (each row is fully read before any of its outputs are
+ * written, and rows are disjoint).
+ */
+#ifndef FARQ_H
+#define FARQ_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FARQ_ABI_VERSION 1
+
+/* Element types. */
+enum farq_dtype {
+    FARQ_DTYPE_BF16 = 0,
+    FARQ_DTYPE_FP16 = 1,
+    FARQ_DTYPE_FP32 = 2,
+    FARQ_DTYPE_INT8 = 3,
+    FARQ_DTYPE_E4M3 = 4
+};
+
+/* flags bits. */
+enum farq_flags {
+    FARQ_FLAG_UE8M0 = 1 /* round every scale up to a power of two (E4M3 only) */
+};
+
+/* Status codes returned by every entry point. Never a device trap. */
+enum farq_status {
+    FARQ_OK = 0,
+    FARQ_ERR_NULL_POINTER = 1,     /* a required pointer is NULL            */
+    FARQ_ERR_BAD_SHAPE = 2,        /* M < 0, D <= 0, D % G != 0, D % 8 != 0  */
+    FARQ_ERR_BAD_GROUP = 3,        /* G not a power of two in [8, 256]       */
+    FARQ_ERR_BAD_DTYPE = 4,        /* unsupported dtype combination          */
+    FARQ_ERR_ALIGNMENT = 5,        /* row base or row stride not 16-B aligned */
+    FARQ_ERR_UNSUPPORTED = 6,      /* D above the supported maximum          */
+    FARQ_ERR_CUDA = 7,             /* a CUDA runtime call failed             */
+    FARQ_ERR_BAD_ARGS_SIZE = 8,    /* struct_size does not match this build  */
+    FARQ_ERR_DEVICE_TIMEOUT = 9    /* a bounded device wait ran out          */
+};
+
+/*
+ * Arguments of one call. Row strides are in ELEMENTS of the tensor they
+ * describe; 0 means "contiguous" (D for the [M,D] tensors, D/G for x_scale).
+ * The inner dimension is always contiguous.
+ *
+ * Replaces the positional arguments of the reference operator
+ * (task01…py:1731-1741). Differences, all extensions:
+ *   - norm_out may be NULL: the normalised tensor is then not written
+ *     (7N + 4N/G + 2D bytes moved instead of 9N + 4N/G + 2D).
+ *   - q_dtype selects INT8 (reference semantics) or E4M3.
+ *   - status, when non-NULL, is a device int the kernel sets to a non-zero
+ *     farq_status if a bounded wait on the device ran out. The kernel never
+ *     clears it; the caller zeroes it.
+ */
+typedef struct farq_args {
+    uint32_t struct_size;          /* = sizeof(farq_args_t)                 */
+    int32_t  x_dtype;              /* BF16 | FP16; residual has the same    */
+    int32_t  gamma_dtype;          /* BF16 | FP16 | FP32                    */
+    int32_t  residual_out_dtype;   /* BF16 | FP16 | FP32                    */
+    int32_t  norm_out_dtype;       /* BF16 | FP16 | FP32 (ignored if NULL)  */
+    int32_t  q_dtype;              /* INT8 | E4M3                           */
+    int32_t  flags;                /* farq_flags                            */
+    int32_t  group_size;           /* G                                     */
+    int64_t  M;                    /* rows (tokens); 0 is a no-op           */
+    int64_t  D;                    /* hidden size                           */
+    float    eps;
+    int32_t  tune_ctas_per_sm;     /* 0 = auto                              */
+    int32_t  tune_stages;          /* 0 = auto                              */
+    int32_t  reserved0;
+    const void* x;                 /* [M, D]                                */
+    const void* residual;          /* [M, D]                                */
+    const void* gamma;             /* [D]                                   */
+    void*    residual_out;         /* [M, D]                                */
+    void*    norm_out;             /* [M, D] or NULL                        */
+    void*    x_q;                  /* [M, D] int8 / e4m3 bytes              */
+    float*   x_scale;              /* [M, D/G] fp32                         */
+    int32_t* status;               /* device int or NULL                    */
+    int64_t  x_row_stride;
+    int64_t  residual_row_stride;
+    int64_t  residual_out_row_stride;
+    int64_t  norm_out_row_stride;
+    int64_t  x_q_row_stride;
+    int64_t  x_scale_row_stride;
+} farq_args_t;
+
+/*
+ * Launch the fused kernel on `stream` (a cudaStream_t; NULL = legacy default
+ * stream) on the current CUDA device. Validates every argument first and
+ * returns a farq_status; on FARQ_OK the work is queued, not finished.
+ * Replaces: fused_add_rmsnorm_group_quant, task01…py:1731-1851 (the routing
+ * at :1772-1817 and :1548-1728 collapses to one kernel with host-chosen
+ * template parameters).
+ */
+int farq_launch(const farq_args_t* args, void* stream);
+
+/* Static string for a farq_status (never NULL). No reference counterpart:
+ * the reference raises whatever Triton raises. */
+const char* farq_strerror(int status);
+
+/* FARQ_ABI_VERSION of the loaded library. No reference counterpart. */
+int farq_abi_version(void);
+
+/* Largest hidden size D farq_launch accepts. The reference's segmented
+ * kernel stops at 4 x 2048 columns (task01…py:1128-1348). */
+int64_t farq_max_hidden(void);
+
+/*
+ * Launch plan the library would use for (M, D, G, x_dtype) on the current
+ * device, written into out[0..4] = {threads per CTA, vectors per thread,
+ * CTAs in the grid, pipeline stages, dynamic shared-memory bytes}.
+ * Host-only query for tests and profiling; launches nothing.
+ * No reference counterpart (Triton picks num_warps at :1772-1817).
+ */
+int farq_plan(int64_t M, int64_t D, int32_t group_size, int32_t x_dtype,
+              int32_t tune_ctas_per_sm, int32_t tune_stages, int64_t out[5]);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FARQ_H */

@@ -1,0 +1,112 @@
+"""The C-ABI library loads and exports every entry point include/farq.h
+declares; argument validation answers with status codes before any device
+work (runs without a GPU)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from flagos_kernelgen_72h_shanghai_2026_b200 import _lib
+from flagos_kernelgen_72h_shanghai_2026_b200._build import LIB_PATH, build_lib
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "farq.h"
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build_lib()
+    return _lib.load()
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return re.findall(r"^\s*(?:int|int64_t|const char\*)\s+(farq_\w+)\s*\(", text, flags=re.M)
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    assert {"farq_launch", "farq_strerror", "farq_abi_version", "farq_max_hidden",
+            "farq_plan"} <= set(names)
+
+
+def test_library_exports_every_declared_symbol(lib):
+    raw = ctypes.CDLL(str(LIB_PATH))
+    for name in declared_functions():
+        assert hasattr(raw, name), f"{name} declared in farq.h but not exported"
+
+
+def test_struct_layout_matches_header(lib):
+    # The header's farq_args_t: 8 x 4-byte fields, 2 x int64, 4 x 4-byte, 8 pointers, 6 int64
+    assert ctypes.sizeof(_lib.FarqArgs) == 8 * 4 + 2 * 8 + 4 * 4 + 8 * 8 + 6 * 8
+    a = _lib.FarqArgs()
+    a.struct_size = ctypes.sizeof(a) + 8
+    assert lib.farq_launch(ctypes.byref(a), None) == _lib.ERR_BAD_ARGS_SIZE
+
+
+def test_version_and_limits(lib):
+    assert lib.farq_abi_version() == _lib.ABI_VERSION
+    assert lib.farq_max_hidden() == 16384
+    for code in range(0, 10):
+        assert lib.farq_strerror(code)
+    assert b"unknown" in lib.farq_strerror(1234)
+
+
+def _args(**kw):
+    a = _lib.FarqArgs()
+    a.struct_size = ctypes.sizeof(a)
+    a.x_dtype = _lib.DTYPE_BF16
+    a.gamma_dtype = _lib.DTYPE_BF16
+    a.residual_out_dtype = _lib.DTYPE_BF16
+    a.norm_out_dtype = _lib.DTYPE_BF16
+    a.q_dtype = _lib.DTYPE_E4M3
+    a.group_size = 128
+    a.M, a.D, a.eps = 4, 1024, 1e-6
+    for k, v in kw.items():
+        setattr(a, k, v)
+    return a
+
+
+@pytest.mark.parametrize("kw,code", [
+    (dict(group_size=96), _lib.ERR_BAD_GROUP),
+    (dict(group_size=4), _lib.ERR_BAD_GROUP),
+    (dict(group_size=512), _lib.ERR_BAD_GROUP),
+    (dict(D=1000), _lib.ERR_BAD_SHAPE),
+    (dict(D=1024 + 64, group_size=128), _lib.ERR_BAD_SHAPE),
+    (dict(M=-1), _lib.ERR_BAD_SHAPE),
+    (dict(D=32768), _lib.ERR_UNSUPPORTED),
+    (dict(x_dtype=_lib.DTYPE_FP32), _lib.ERR_BAD_DTYPE),
+    (dict(q_dtype=_lib.DTYPE_BF16), _lib.ERR_BAD_DTYPE),
+    (dict(gamma_dtype=_lib.DTYPE_INT8), _lib.ERR_BAD_DTYPE),
+    (dict(), _lib.ERR_NULL_POINTER),
+])
+def test_validation_codes(lib, kw, code):
+    assert lib.farq_launch(ctypes.byref(_args(**kw)), None) == code
+
+
+def test_m_zero_is_a_noop(lib):
+    assert lib.farq_launch(ctypes.byref(_args(M=0)), None) == _lib.OK
+
+
+def test_misaligned_pointer_rejected(lib):
+    a = _args(x=0x1008, residual=0x2000, gamma=0x3000, residual_out=0x4000,
+              x_q=0x5000, x_scale=0x6000)
+    assert lib.farq_launch(ctypes.byref(a), None) == _lib.ERR_ALIGNMENT
+    a = _args(x=0x1000, residual=0x2000, gamma=0x3000, residual_out=0x4000,
+              x_q=0x5000, x_scale=0x6000, x_row_stride=1028)
+    assert lib.farq_launch(ctypes.byref(a), None) == _lib.ERR_ALIGNMENT
+
+
+def test_null_args_pointer(lib):
+    assert lib.farq_launch(None, None) == _lib.ERR_NULL_POINTER
+
+
+def test_python_wrapper_refuses_cpu_tensors():
+    from flagos_kernelgen_72h_shanghai_2026_b200 import fused_add_rmsnorm_group_quant
+    x = torch.zeros(2, 256, dtype=torch.bfloat16)
+    with pytest.raises(TypeError, match="CUDA"):
+        fused_add_rmsnorm_group_quant(x, x, torch.ones(256, dtype=torch.bfloat16), x.clone(), None,
+                                      torch.zeros(2, 256, dtype=torch.int8),
+                                      torch.zeros(2, 2), 1e-6, 128)
