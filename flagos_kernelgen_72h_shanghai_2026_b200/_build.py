@@ -15,15 +15,15 @@ PKG_DIR = Path(__file__).resolve().parent
 REPO_DIR = PKG_DIR.parent
 INCLUDE_DIR = REPO_DIR / "include"
 CSRC_DIR = PKG_DIR / "csrc"
-SOURCES = [CSRC_DIR / "farq.cu"]
-HEADERS = [INCLUDE_DIR / "farq.h"]
+SOURCES = [CSRC_DIR / "farq.cu", *sorted(CSRC_DIR.glob("farq_inst_*.cu"))]
+HEADERS = [INCLUDE_DIR / "farq.h", CSRC_DIR / "farq_kernel.cuh"]
 LIB_PATH = PKG_DIR / "libfarq.so"
 
-NVCC_FLAGS = [
-    "-gencode", "arch=compute_100a,code=sm_100a",
-    "-lineinfo", "-O3", "-std=c++17",
-    "-shared", "-Xcompiler", "-fPIC,-O3",
-]
+OBJ_DIR = PKG_DIR / "_build"
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = [*ARCH, "-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC,-O3"]
+LINK_FLAGS = [*ARCH, "-shared", "-Xcompiler", "-fPIC"]
 
 
 def _nvcc() -> str:
@@ -40,20 +40,41 @@ def is_stale() -> bool:
     return any(p.stat().st_mtime > t for p in SOURCES + HEADERS)
 
 
-def build_lib(force: bool = False, verbose: bool = False) -> Path:
-    """Compile libfarq.so for sm_100a if it is missing or older than its sources."""
-    if not force and not is_stale():
-        return LIB_PATH
-    tmp = LIB_PATH.with_suffix(".so.tmp")
-    cmd = [_nvcc(), *NVCC_FLAGS, f"-I{INCLUDE_DIR}", "-o", str(tmp), *map(str, SOURCES)]
+def _run(cmd: list[str], verbose: bool) -> str:
     if verbose:
-        cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd))
     res = subprocess.run(cmd, capture_output=True, text=True)
     if res.returncode != 0:
-        raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
-    if verbose and res.stderr:
-        print(res.stderr)
+        raise RuntimeError(f"nvcc failed ({res.returncode}):\n{' '.join(cmd)}\n{res.stdout}\n{res.stderr}")
+    return res.stderr
+
+
+def build_lib(force: bool = False, verbose: bool = False) -> Path:
+    """Compile libfarq.so for sm_100a if it is missing or older than its sources.
+
+    Each translation unit is compiled to an object in parallel (the kernel
+    instantiations dominate), then linked into one shared library."""
+    if not force and not is_stale():
+        return LIB_PATH
+    from concurrent.futures import ThreadPoolExecutor
+
+    nvcc = _nvcc()
+    OBJ_DIR.mkdir(exist_ok=True)
+    flags = [*NVCC_FLAGS, f"-I{INCLUDE_DIR}", f"-I{CSRC_DIR}"]
+    if verbose:
+        flags.append("-Xptxas=-v")
+    jobs = []
+    for src in SOURCES:
+        obj = OBJ_DIR / (src.stem + ".o")
+        jobs.append(([nvcc, *flags, "-c", "-o", str(obj), str(src)], obj))
+    with ThreadPoolExecutor(max_workers=min(len(jobs), os.cpu_count() or 1)) as ex:
+        logs = list(ex.map(lambda j: _run(j[0], verbose), jobs))
+    if verbose:
+        for log in logs:
+            if log:
+                print(log)
+    tmp = LIB_PATH.with_suffix(".so.tmp")
+    _run([nvcc, *LINK_FLAGS, "-o", str(tmp), *(str(o) for _, o in jobs)], verbose)
     os.replace(tmp, LIB_PATH)
     return LIB_PATH
 

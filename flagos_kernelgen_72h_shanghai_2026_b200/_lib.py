@@ -47,7 +47,9 @@ class FarqArgs(ctypes.Structure):
         ("D", ctypes.c_int64),
         ("eps", ctypes.c_float),
         ("tune_ctas_per_sm", ctypes.c_int32),
+        ("tune_teams_per_cta", ctypes.c_int32),
         ("tune_stages", ctypes.c_int32),
+        ("tune_vec_per_thread", ctypes.c_int32),
         ("reserved0", ctypes.c_int32),
         ("x", ctypes.c_void_p),
         ("residual", ctypes.c_void_p),
@@ -94,7 +96,8 @@ def load(path: Path | str | None = None) -> ctypes.CDLL:
         lib.farq_max_hidden.argtypes = []
         lib.farq_max_hidden.restype = ctypes.c_int64
         lib.farq_plan.argtypes = [ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
-                                  ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(ctypes.c_int64)]
+                                  ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+                                  ctypes.POINTER(ctypes.c_int64)]
         lib.farq_plan.restype = ctypes.c_int
         v = lib.farq_abi_version()
         if v != ABI_VERSION:
@@ -108,11 +111,13 @@ def strerror(status: int) -> str:
     return load().farq_strerror(status).decode()
 
 
-def plan(M: int, D: int, group_size: int, x_dtype: int, ctas_per_sm: int = 0,
-         stages: int = 0) -> dict:
+def plan(M: int, D: int, group_size: int, x_dtype: int, ctas_per_sm: int = 0, teams: int = 0,
+         stages: int = 0, vec_per_thread: int = 0) -> dict:
     """The launch plan farq_launch would use on the current device."""
-    out = (ctypes.c_int64 * 5)()
-    st = load().farq_plan(M, D, group_size, x_dtype, ctas_per_sm, stages, out)
+    out = (ctypes.c_int64 * 6)()
+    st = load().farq_plan(M, D, group_size, x_dtype, ctas_per_sm, teams, stages, vec_per_thread,
+                          out)
     if st != OK:
         raise RuntimeError(f"farq_plan: {strerror(st)}")
-    return dict(threads=out[0], vec_per_thread=out[1], grid=out[2], stages=out[3], smem=out[4])
+    return dict(team_threads=out[0], teams=out[1], vec_per_thread=out[2], grid=out[3],
+                stages=out[4], smem=out[5])

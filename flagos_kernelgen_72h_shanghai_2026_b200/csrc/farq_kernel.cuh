@@ -1,0 +1,456 @@
+// farq_kernel.cuh — device code of the B200 (sm_100a) fused residual-add +
+// RMSNorm + per-token group quantisation kernel (C ABI: include/farq.h).
+//
+// Reference behaviour (sinpeyw/flagos-kernelgen-72h-shanghai-2026,
+// src/task01_fused_add_rmsnorm_group_quant.py):
+//   per-row math ............ :65-121 (full row), :1127-1348 (segmented),
+//                             :1401-1546 (two rows per program)
+//   quantisation ............ :1089-1104  scale = max(gmax*(inv/127), 1e-12),
+//                                         q = trunc(clamp(norm*(1/scale), ±127))
+//   reduction ............... :1274-1278  inv = rsqrt(sum(r*r)/D + eps)
+//
+// Execution model (one kernel for every shape the reference routes separately):
+//   * A CTA holds `teams` independent row teams of T threads (T a multiple of
+//     32). Team j of CTA b owns rows tg, tg + ntot, ... with tg = b*teams + j
+//     and ntot = grid*teams. Teams synchronise only among themselves, on
+//     named barrier 1 + j, so one team's reduction never stalls another.
+//   * gamma is converted to fp32 once per CTA into shared memory.
+//   * Each team has `stages` shared-memory slots; a row of x and one of
+//     residual enter a slot by two cp.async.bulk copies (TMA engine, no
+//     multicast) that complete on the slot's mbarrier.
+//   * Thread t of a team owns the 16-byte vectors v = k*T + t, k < K, of a
+//     row. Phase 1: r = x + residual (fp32), residual_out written once,
+//     sum(r*r) in fp64, w = r*gamma kept in registers, per-group absmax by
+//     xor-shuffles over the GL = G/8 lanes of a group. One team barrier
+//     reduces sum(r*r); right after it the slot is refilled with the team's
+//     next row, so the copy overlaps phase 2. Phase 2: norm = w*inv_rms,
+//     scale, q (int8 truncation or e4m3 RNE with saturation).
+//   * sum(r*r) is accumulated in fp64 (exact squares of fp32 values, error
+//     ~1e-16 relative) and rounded to fp32 once, so inv_rms does not depend
+//     on the summation order. With fp32 accumulation every ulp of inv_rms
+//     flips a group-maximum element (which sits on ±QMAX mathematically)
+//     between two codes, on ~1/(2G) of all elements.
+//   * Every device-side wait is bounded; a wait that runs out sets the
+//     caller's status word, and the team drains its copies and returns.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "farq.h"
+
+namespace farq {
+
+constexpr int kMaxK = 8;              // 16-byte vectors per thread per row
+constexpr int kMaxCtaThreads = 512;   // threads per CTA (launch bound)
+constexpr int kMaxTeamThreads = 512;  // threads per row team
+constexpr int kMaxTeamWarps = kMaxTeamThreads / 32;
+// Largest D: gamma (4D bytes) and one slot (4D bytes for 2-byte inputs) must
+// fit the 227 KB of shared memory a CTA may use.
+constexpr int64_t kMaxHidden = 16384;
+constexpr int kMaxStages = 4;
+constexpr int kMaxTeams = 15;         // named barriers 1..15
+constexpr uint32_t kSpinLimit = 1u << 26;  // bounded mbarrier polls
+
+struct Params {
+  const uint8_t* x;
+  const uint8_t* res;
+  const void* gamma;
+  uint8_t* rout;
+  uint8_t* nout;     // may be null
+  uint8_t* q;
+  float* scale;
+  int32_t* status;   // may be null
+  int64_t M;
+  int64_t sx, sr, sro, sno, sq, ss;  // row strides in bytes (ss: in floats)
+  int32_t D;
+  int32_t nvec;      // D / 8
+  int32_t team_threads;
+  int32_t teams;
+  int32_t stages;
+  uint32_t row_bytes;  // D * sizeof(x element)
+  int32_t gamma_dtype, rout_dtype, nout_dtype;
+  int32_t ue8m0;
+  float eps;
+};
+
+// Shared-memory carve-up, identical on host and device.
+struct SmemLayout {
+  size_t gamma, stages, bars, red, total;
+};
+__host__ __device__ inline SmemLayout smem_layout(int D, uint32_t row_bytes, int teams,
+                                                  int stages) {
+  SmemLayout L;
+  L.gamma = 0;
+  L.stages = (size_t)D * sizeof(float);                       // multiple of 32
+  L.bars = L.stages + (size_t)teams * stages * 2 * row_bytes;  // multiple of 32
+  L.red = L.bars + (size_t)teams * stages * sizeof(uint64_t);
+  L.total = L.red + (size_t)teams * kMaxTeamWarps * sizeof(double);
+  return L;
+}
+
+// ---------------------------------------------------------------- PTX helpers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: true when the phase completed, false when the poll limit ran out.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+// Global -> shared bulk copy through the TMA engine into this CTA's own
+// shared memory, completion counted in bytes on `bar`.
+__device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes,
+                                          uint32_t bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(dst),
+      "l"(src), "r"(bytes), "r"(bar), "l"(pol)
+      : "memory");
+}
+// Named barrier over `count` threads.
+__device__ __forceinline__ void team_sync(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+// Named barrier that also ORs a predicate over the participating threads.
+__device__ __forceinline__ bool team_sync_or(uint32_t id, uint32_t count, bool flag) {
+  uint32_t any;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 q, %1, 0;\n\t"
+      "bar.red.or.pred p, %2, %3, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(any)
+      : "r"((uint32_t)flag), "r"(id), "r"(count)
+      : "memory");
+  return any != 0;
+}
+__device__ __forceinline__ void st_cs_v4(void* p, uint4 v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ void st_cs_v2(void* p, uint32_t a, uint32_t b) {
+  asm volatile("st.global.cs.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(a), "r"(b) : "memory");
+}
+__device__ __forceinline__ void st_cs_f32(float* p, float v) {
+  asm volatile("st.global.cs.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
+
+// ------------------------------------------------------------ element formats
+template <typename T>
+struct Unpack;
+template <>
+struct Unpack<__nv_bfloat16> {
+  // 8 bf16 -> 8 fp32: a bf16 is the top half of the fp32 with the same value.
+  __device__ __forceinline__ static void run(const uint4 v, float f[8]) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = __uint_as_float(w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+    }
+  }
+};
+template <>
+struct Unpack<__half> {
+  __device__ __forceinline__ static void run(const uint4 v, float f[8]) {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 t = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+      f[2 * i] = t.x;
+      f[2 * i + 1] = t.y;
+    }
+  }
+};
+
+__device__ __forceinline__ uint32_t pack2(float a, float b, int dtype) {
+  if (dtype == FARQ_DTYPE_BF16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+// Store 8 fp32 values as `dtype` (BF16/FP16 round-to-nearest-even, or FP32)
+// at element offset 8*v of the row that starts at `row`.
+__device__ __forceinline__ void store8(uint8_t* row, int v, const float f[8], int dtype) {
+  if (dtype == FARQ_DTYPE_FP32) {
+    float* p = reinterpret_cast<float*>(row) + 8 * (int64_t)v;
+    st_cs_v4(p, make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
+                           __float_as_uint(f[3])));
+    st_cs_v4(p + 4, make_uint4(__float_as_uint(f[4]), __float_as_uint(f[5]),
+                               __float_as_uint(f[6]), __float_as_uint(f[7])));
+  } else {
+    uint4 o;
+    o.x = pack2(f[0], f[1], dtype);
+    o.y = pack2(f[2], f[3], dtype);
+    o.z = pack2(f[4], f[5], dtype);
+    o.w = pack2(f[6], f[7], dtype);
+    st_cs_v4(row + 16 * (int64_t)v, o);
+  }
+}
+__device__ __forceinline__ void load_gamma8(const void* g, int v, int dtype, float f[8]) {
+  if (dtype == FARQ_DTYPE_FP32) {
+    const float4* p = reinterpret_cast<const float4*>(g) + 2 * (int64_t)v;
+    const float4 a = __ldg(p), b = __ldg(p + 1);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
+    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  } else {
+    const uint4 raw = __ldg(reinterpret_cast<const uint4*>(g) + v);
+    if (dtype == FARQ_DTYPE_BF16)
+      Unpack<__nv_bfloat16>::run(raw, f);
+    else
+      Unpack<__half>::run(raw, f);
+  }
+}
+// Two fp32 -> two e4m3 bytes (low byte = lo), round-to-nearest-even,
+// saturating to ±448.
+__device__ __forceinline__ uint32_t e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ uint32_t i8(float v) {
+  v = fminf(fmaxf(v, -127.0f), 127.0f);
+  return static_cast<uint32_t>(__float2int_rz(v)) & 0xffu;
+}
+// Round a positive normal fp32 up to the next power of two (identity on
+// powers of two): clear the mantissa, bump the exponent if it was non-zero.
+__device__ __forceinline__ float pow2_ceil(float s) {
+  uint32_t b = __float_as_uint(s);
+  if (b & 0x007fffffu) b = (b & 0xff800000u) + 0x00800000u;
+  return __uint_as_float(b);
+}
+
+// -------------------------------------------------------------------- kernel
+template <typename Tin, int K, int GL, bool E4M3>
+__global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_rows_kernel(const Params p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const SmemLayout L = smem_layout(p.D, p.row_bytes, p.teams, p.stages);
+  const int T = p.team_threads;
+  const int team = threadIdx.x / T;
+  const int tt = threadIdx.x - team * T;
+  const int lane = threadIdx.x & 31;
+  const int twarp = tt >> 5;
+  const int S = p.stages;
+  const uint32_t stage_bytes = 2u * p.row_bytes;
+  const uint32_t bar_id = 1u + (uint32_t)team;
+
+  const float4* sg = reinterpret_cast<const float4*>(smem + L.gamma);
+  uint8_t* my_stage0 = smem + L.stages + (size_t)team * S * stage_bytes;
+  uint64_t* my_bars = reinterpret_cast<uint64_t*>(smem + L.bars) + team * S;
+  double* my_red = reinterpret_cast<double*>(smem + L.red) + team * kMaxTeamWarps;
+
+  const int64_t tg = (int64_t)blockIdx.x * p.teams + team;
+  const int64_t ntot = (int64_t)gridDim.x * p.teams;
+  const int64_t nrows = tg < p.M ? (p.M - 1 - tg) / ntot + 1 : 0;
+
+  uint64_t pol = 0;
+  int64_t issued = 0;  // rows queued by this team (thread 0 of the team only)
+  if (tt == 0) {
+    pol = policy_evict_first();
+    for (int s = 0; s < S; ++s) mbar_init(smem_u32(&my_bars[s]), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    for (; issued < nrows && issued < S; ++issued) {
+      const int64_t row = tg + issued * ntot;
+      const uint32_t bar = smem_u32(&my_bars[issued]);
+      const uint32_t dst = smem_u32(my_stage0 + (size_t)issued * stage_bytes);
+      mbar_arrive_expect_tx(bar, stage_bytes);
+      bulk_load(dst, p.x + row * p.sx, p.row_bytes, bar, pol);
+      bulk_load(dst + p.row_bytes, p.res + row * p.sr, p.row_bytes, bar, pol);
+    }
+  }
+  // gamma -> fp32 shared memory, once per CTA (overlaps the first copies).
+  for (int v = threadIdx.x; v < p.nvec; v += blockDim.x) {
+    float g[8];
+    load_gamma8(p.gamma, v, p.gamma_dtype, g);
+    float4* d = reinterpret_cast<float4*>(smem + L.gamma) + 2 * v;
+    d[0] = make_float4(g[0], g[1], g[2], g[3]);
+    d[1] = make_float4(g[4], g[5], g[6], g[7]);
+  }
+  __syncthreads();
+  if (nrows == 0) return;
+
+  const float qmax = E4M3 ? 448.0f : 127.0f;
+  const int nvec = p.nvec;
+  const int tw = T >> 5;
+  int64_t consumed = nrows;
+  bool aborted = false;
+
+  for (int64_t i = 0; i < nrows; ++i) {
+    const int s = (int)(i % S);
+    const uint32_t parity = (uint32_t)((i / S) & 1);
+    const bool ok = mbar_wait_bounded(smem_u32(&my_bars[s]), parity);
+    if (team_sync_or(bar_id, T, !ok)) {
+      if (tt == 0 && p.status) atomicExch(p.status, (int)FARQ_ERR_DEVICE_TIMEOUT);
+      consumed = i;
+      aborted = true;
+      break;
+    }
+    const int64_t row = tg + i * ntot;
+    const uint8_t* sx = my_stage0 + (size_t)s * stage_bytes;
+    const uint8_t* sr = sx + p.row_bytes;
+    uint8_t* rout_row = p.rout + row * p.sro;
+
+    // ---- phase 1
+    float w[K][8];
+    float gmax[K];
+    double ss0 = 0.0, ss1 = 0.0;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int v = k * T + tt;
+      float m = 0.f;
+      if (v < nvec) {
+        float a[8], b[8];
+        Unpack<Tin>::run(reinterpret_cast<const uint4*>(sx)[v], a);
+        Unpack<Tin>::run(reinterpret_cast<const uint4*>(sr)[v], b);
+        const float4 g0 = sg[2 * v], g1 = sg[2 * v + 1];
+        const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          a[e] = a[e] + b[e];
+          if (e & 1)
+            ss1 = fma((double)a[e], (double)a[e], ss1);
+          else
+            ss0 = fma((double)a[e], (double)a[e], ss0);
+          w[k][e] = a[e] * g[e];
+          m = fmaxf(m, fabsf(w[k][e]));
+        }
+        store8(rout_row, v, a, p.rout_dtype);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) w[k][e] = 0.f;
+      }
+#pragma unroll
+      for (int o = 1; o < GL; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      gmax[k] = m;
+    }
+    double ss = ss0 + ss1;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) my_red[twarp] = ss;
+    team_sync(bar_id, T);
+
+    // The slot is no longer read: queue the team's row that uses it next.
+    if (tt == 0 && issued < nrows) {
+      const int64_t nrow = tg + issued * ntot;
+      const uint32_t bar = smem_u32(&my_bars[s]);
+      const uint32_t dst = smem_u32(my_stage0 + (size_t)s * stage_bytes);
+      mbar_arrive_expect_tx(bar, stage_bytes);
+      bulk_load(dst, p.x + nrow * p.sx, p.row_bytes, bar, pol);
+      bulk_load(dst + p.row_bytes, p.res + nrow * p.sr, p.row_bytes, bar, pol);
+      ++issued;
+    }
+
+    double total = 0.0;
+    for (int j = 0; j < tw; ++j) total += my_red[j];
+    const float inv_rms =
+        __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(__double2float_rn(total), (float)p.D), p.eps)));
+    const float step = __fdiv_rn(inv_rms, qmax);
+
+    // ---- phase 2
+    uint8_t* nout_row = p.nout ? p.nout + row * p.sno : nullptr;
+    uint8_t* q_row = p.q + row * p.sq;
+    float* sc_row = p.scale + row * p.ss;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int v = k * T + tt;
+      if (v < nvec) {
+        float sc = fmaxf(gmax[k] * step, 1.0e-12f);
+        if (p.ue8m0) sc = pow2_ceil(sc);
+        const float isc = __frcp_rn(sc);
+        float nrm[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) nrm[e] = w[k][e] * inv_rms;
+        if (nout_row) store8(nout_row, v, nrm, p.nout_dtype);
+        uint32_t lo, hi;
+        if (E4M3) {
+          lo = e4m3x2(nrm[0] * isc, nrm[1] * isc) | (e4m3x2(nrm[2] * isc, nrm[3] * isc) << 16);
+          hi = e4m3x2(nrm[4] * isc, nrm[5] * isc) | (e4m3x2(nrm[6] * isc, nrm[7] * isc) << 16);
+        } else {
+          lo = i8(nrm[0] * isc) | (i8(nrm[1] * isc) << 8) | (i8(nrm[2] * isc) << 16) |
+               (i8(nrm[3] * isc) << 24);
+          hi = i8(nrm[4] * isc) | (i8(nrm[5] * isc) << 8) | (i8(nrm[6] * isc) << 16) |
+               (i8(nrm[7] * isc) << 24);
+        }
+        st_cs_v2(q_row + 8 * (int64_t)v, lo, hi);
+        if ((lane & (GL - 1)) == 0) st_cs_f32(sc_row + v / GL, sc);
+      }
+    }
+  }
+
+  // Abort path: no bulk copy may still target this team's shared memory
+  // when the CTA exits. Copies for rows [consumed, issued) may be in flight.
+  if (aborted && tt == 0) {
+    for (int64_t j = consumed; j < issued; ++j)
+      (void)mbar_wait_bounded(smem_u32(&my_bars[j % S]), (uint32_t)((j / S) & 1));
+  }
+}
+
+using KernelFn = void (*)(const Params);
+
+// Kernel table of one (input dtype, quantised dtype) pair, indexed by
+// K (1..kMaxK) and log2(GL) (0..5). Defined in farq_inst_*.cu.
+KernelFn kernel_bf16_int8(int K, int gl_log2);
+KernelFn kernel_bf16_e4m3(int K, int gl_log2);
+KernelFn kernel_fp16_int8(int K, int gl_log2);
+KernelFn kernel_fp16_e4m3(int K, int gl_log2);
+
+}  // namespace farq
+
+// Instantiates the kernel table of one (Tin, E4M3) pair.
+#define FARQ_KERNEL_TABLE(NAME, TIN, E4M3)                                              \
+  namespace farq {                                                                      \
+  template <int K>                                                                      \
+  static KernelFn NAME##_k(int gl_log2) {                                               \
+    switch (gl_log2) {                                                                  \
+      case 0: return farq_rows_kernel<TIN, K, 1, E4M3>;                                 \
+      case 1: return farq_rows_kernel<TIN, K, 2, E4M3>;                                 \
+      case 2: return farq_rows_kernel<TIN, K, 4, E4M3>;                                 \
+      case 3: return farq_rows_kernel<TIN, K, 8, E4M3>;                                 \
+      case 4: return farq_rows_kernel<TIN, K, 16, E4M3>;                                \
+      default: return farq_rows_kernel<TIN, K, 32, E4M3>;                               \
+    }                                                                                   \
+  }                                                                                     \
+  KernelFn NAME(int K, int gl_log2) {                                                   \
+    switch (K) {                                                                        \
+      case 1: return NAME##_k<1>(gl_log2);                                              \
+      case 2: return NAME##_k<2>(gl_log2);                                              \
+      case 3: return NAME##_k<3>(gl_log2);                                              \
+      case 4: return NAME##_k<4>(gl_log2);                                              \
+      case 5: return NAME##_k<5>(gl_log2);                                              \
+      case 6: return NAME##_k<6>(gl_log2);                                              \
+      case 7: return NAME##_k<7>(gl_log2);                                              \
+      default: return NAME##_k<8>(gl_log2);                                             \
+    }                                                                                   \
+  }                                                                                     \
+  }

@@ -75,7 +75,9 @@ def fused_add_rmsnorm_group_quant(
     *,
     ue8m0: bool = False,
     _tune_ctas_per_sm: int = 0,
+    _tune_teams_per_cta: int = 0,
     _tune_stages: int = 0,
+    _tune_vec_per_thread: int = 0,
     _status: torch.Tensor | None = None,
 ):
     """residual_out = x + residual; norm = RMSNorm(residual_out) * gamma;
@@ -146,7 +148,9 @@ def fused_add_rmsnorm_group_quant(
     a.D = D
     a.eps = float(eps)
     a.tune_ctas_per_sm = int(_tune_ctas_per_sm)
+    a.tune_teams_per_cta = int(_tune_teams_per_cta)
     a.tune_stages = int(_tune_stages)
+    a.tune_vec_per_thread = int(_tune_vec_per_thread)
     a.x = x.data_ptr()
     a.residual = residual.data_ptr()
     a.gamma = gamma.data_ptr()
@@ -179,6 +183,9 @@ def fused_add_rmsnorm_group_quant(
 
 
 def launch_plan(M: int, D: int, group_size: int = 128, dtype: torch.dtype = torch.bfloat16,
-                ctas_per_sm: int = 0, stages: int = 0) -> dict:
-    """Launch plan (threads, vectors per thread, grid, stages, smem bytes) on the current device."""
-    return _lib.plan(M, D, group_size, _IN_DTYPES[dtype], ctas_per_sm, stages)
+                ctas_per_sm: int = 0, teams: int = 0, stages: int = 0,
+                vec_per_thread: int = 0) -> dict:
+    """Launch plan (team threads, teams per CTA, vectors per thread, grid,
+    slots per team, shared-memory bytes) on the current device."""
+    return _lib.plan(M, D, group_size, _IN_DTYPES[dtype], ctas_per_sm, teams, stages,
+                     vec_per_thread)

@@ -62,7 +62,7 @@ enum farq_status {
     FARQ_ERR_BAD_GROUP = 3,        /* G not a power of two in [8, 256]       */
     FARQ_ERR_BAD_DTYPE = 4,        /* unsupported dtype combination          */
     FARQ_ERR_ALIGNMENT = 5,        /* row base or row stride not 16-B aligned */
-    FARQ_ERR_UNSUPPORTED = 6,      /* D above the supported maximum          */
+    FARQ_ERR_UNSUPPORTED = 6,      /* D or a tuning choice out of range      */
     FARQ_ERR_CUDA = 7,             /* a CUDA runtime call failed             */
     FARQ_ERR_BAD_ARGS_SIZE = 8,    /* struct_size does not match this build  */
     FARQ_ERR_DEVICE_TIMEOUT = 9    /* a bounded device wait ran out          */
@@ -94,9 +94,11 @@ typedef struct farq_args {
     int64_t  M;                    /* rows (tokens); 0 is a no-op           */
     int64_t  D;                    /* hidden size                           */
     float    eps;
-    int32_t  tune_ctas_per_sm;     /* 0 = auto                              */
-    int32_t  tune_stages;          /* 0 = auto                              */
-    int32_t  reserved0;
+    int32_t  tune_ctas_per_sm;     /* 0 = auto (1)                          */
+    int32_t  tune_teams_per_cta;   /* 0 = auto; upper bound on row teams    */
+    int32_t  tune_stages;          /* 0 = auto; shared-memory slots per team */
+    int32_t  tune_vec_per_thread;  /* 0 = auto; 1..8 16-byte vectors        */
+    int32_t  reserved0;            /* must be 0                             */
     const void* x;                 /* [M, D]                                */
     const void* residual;          /* [M, D]                                */
     const void* gamma;             /* [D]                                   */
@@ -136,13 +138,15 @@ int64_t farq_max_hidden(void);
 
 /*
  * Launch plan the library would use for (M, D, G, x_dtype) on the current
- * device, written into out[0..4] = {threads per CTA, vectors per thread,
- * CTAs in the grid, pipeline stages, dynamic shared-memory bytes}.
- * Host-only query for tests and profiling; launches nothing.
- * No reference counterpart (Triton picks num_warps at :1772-1817).
+ * device, written into out[0..5] = {threads per row team, row teams per CTA,
+ * 16-byte vectors per thread, CTAs in the grid, pipeline slots per team,
+ * dynamic shared-memory bytes}. Host-only query for tests and profiling;
+ * launches nothing. No reference counterpart (Triton picks num_warps and the
+ * kernel at task01…py:1772-1817).
  */
 int farq_plan(int64_t M, int64_t D, int32_t group_size, int32_t x_dtype,
-              int32_t tune_ctas_per_sm, int32_t tune_stages, int64_t out[5]);
+              int32_t tune_ctas_per_sm, int32_t tune_teams_per_cta,
+              int32_t tune_stages, int32_t tune_vec_per_thread, int64_t out[6]);
 
 #ifdef __cplusplus
 }

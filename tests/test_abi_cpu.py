@@ -39,8 +39,8 @@ def test_library_exports_every_declared_symbol(lib):
 
 
 def test_struct_layout_matches_header(lib):
-    # The header's farq_args_t: 8 x 4-byte fields, 2 x int64, 4 x 4-byte, 8 pointers, 6 int64
-    assert ctypes.sizeof(_lib.FarqArgs) == 8 * 4 + 2 * 8 + 4 * 4 + 8 * 8 + 6 * 8
+    # The header's farq_args_t: 8 x 4-byte fields, 2 x int64, 6 x 4-byte, 8 pointers, 6 int64
+    assert ctypes.sizeof(_lib.FarqArgs) == 8 * 4 + 2 * 8 + 6 * 4 + 8 * 8 + 6 * 8
     a = _lib.FarqArgs()
     a.struct_size = ctypes.sizeof(a) + 8
     assert lib.farq_launch(ctypes.byref(a), None) == _lib.ERR_BAD_ARGS_SIZE

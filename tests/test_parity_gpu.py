@@ -234,11 +234,15 @@ def test_tuning_knobs_do_not_change_results(cuda_dev):
     w = Workload("t", 1000, 7168, seed=19)
     x, r, g = make_inputs(w)
     base = run_gpu(x, r, g, w.eps, 128, torch.float8_e4m3fn, cuda_dev)
-    for ctas, stages in ((1, 1), (1, 2), (2, 1), (1, 7), (2, 3), (3, 2)):
+    for ctas, teams, stages, k in ((1, 1, 1, 0), (1, 4, 2, 0), (2, 1, 1, 0), (1, 2, 3, 0),
+                                   (1, 0, 0, 4), (1, 0, 0, 8), (2, 2, 1, 2), (1, 3, 2, 5)):
         got = run_gpu(x, r, g, w.eps, 128, torch.float8_e4m3fn, cuda_dev,
-                      _tune_ctas_per_sm=ctas, _tune_stages=stages)
-        for k in base:
-            assert torch.equal(got[k].view(torch.uint8), base[k].view(torch.uint8)), (ctas, stages, k)
+                      _tune_ctas_per_sm=ctas, _tune_teams_per_cta=teams, _tune_stages=stages,
+                      _tune_vec_per_thread=k)
+        for key in base:
+            if base[key] is not None:
+                assert torch.equal(got[key].view(torch.uint8), base[key].view(torch.uint8)), \
+                    (ctas, teams, stages, k, key)
 
 
 def test_side_stream_and_cuda_graph(cuda_dev):
@@ -299,6 +303,7 @@ def test_errors_raise(cuda_dev):
 def test_launch_plan_reports_persistent_grid(cuda_dev):
     p = launch_plan(4096, 7168)
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    assert p["threads"] == 224 and p["vec_per_thread"] == 4
-    assert p["grid"] % sms == 0 and p["stages"] >= 2
-    assert launch_plan(5, 7168)["grid"] == 5
+    assert p["team_threads"] * p["vec_per_thread"] * 8 >= 7168
+    assert p["grid"] == sms and p["teams"] >= 1 and p["stages"] >= 1
+    small = launch_plan(5, 7168)
+    assert small["grid"] == 5 and small["teams"] == 1
