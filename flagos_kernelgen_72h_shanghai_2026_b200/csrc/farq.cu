@@ -132,32 +132,28 @@ int make_plan(int64_t M, int64_t D, int x_dtype, int sms, int smem_optin, int re
   auto fits = [&](int teams, int stages) {
     return (int64_t)smem_layout((int)D, row_bytes, teams, stages).total <= smem_cap;
   };
-  auto max_teams = [&](int stages) {
-    int t = teams_cap;
-    while (t > 0 && !fits(t, stages)) --t;
-    return t;
+  // Ring slots that fit next to gamma (at most kMaxStages).
+  auto max_slots = [&](int teams) {
+    int s = kMaxStages;
+    while (s > 0 && !fits(teams, s)) --s;
+    return s;
   };
-  int teams, stages;
-  if (tune.stages > 0) {
-    stages = tune.stages > kMaxStages ? kMaxStages : tune.stages;
-    teams = max_teams(stages);
-  } else {
-    // Prefer two slots per team (the next row's copy overlaps the current
-    // row's phase 1 as well as phase 2) unless that costs teams.
-    const int t2 = max_teams(2), t1 = max_teams(1);
-    if (t2 >= t1 && t2 > 0) {
-      teams = t2;
-      stages = 2;
-    } else {
-      teams = t1;
-      stages = 1;
-    }
-  }
-  if (teams < 1) return FARQ_ERR_UNSUPPORTED;
+  int teams = teams_cap;
   if (tune.teams > 0 && tune.teams < teams) teams = tune.teams;
   // Small M: spread rows over SMs before stacking teams on one SM.
   const int64_t per_sm = (M + (int64_t)sms * ctas - 1) / ((int64_t)sms * ctas);
   if (per_sm < teams) teams = (int)(per_sm < 1 ? 1 : per_sm);
+  // Every team needs a slot of its own (S >= teams).
+  while (teams > 1 && max_slots(teams) < teams) --teams;
+  // Default ring: one slot per team. More slots keep more rows in flight but
+  // measured slower on B200 (4 teams: 4 slots 39.7 us, 7 slots 42.9 us at
+  // 4096 x 7168), so extra slots are opt-in through tune.stages.
+  int stages = max_slots(teams);
+  if (stages > teams) stages = teams;
+  const int slots_fit = max_slots(teams);
+  if (tune.stages > 0)  // requested ring slots, clamped to [teams, what fits]
+    stages = tune.stages < teams ? teams : (tune.stages < slots_fit ? tune.stages : slots_fit);
+  if (stages < 1 || stages < teams) return FARQ_ERR_UNSUPPORTED;
   int64_t grid = (M + teams - 1) / teams;
   if (grid > (int64_t)sms * ctas) grid = (int64_t)sms * ctas;
   if (grid < 1) grid = 1;

@@ -11,19 +11,23 @@
 //
 // Execution model (one kernel for every shape the reference routes separately):
 //   * A CTA holds `teams` independent row teams of T threads (T a multiple of
-//     32). Team j of CTA b owns rows tg, tg + ntot, ... with tg = b*teams + j
-//     and ntot = grid*teams. Teams synchronise only among themselves, on
-//     named barrier 1 + j, so one team's reduction never stalls another.
+//     32) and a ring of S >= teams shared-memory slots. CTA-local row n
+//     (global row blockIdx.x + n*grid) goes to slot n % S and team n % teams.
+//     A row of x and one of residual enter a slot by two cp.async.bulk copies
+//     (TMA engine, no multicast) that complete on the slot's mbarrier.
+//   * Teams synchronise only among themselves, on named barrier 1 + team, so
+//     one team's reduction never stalls another. When a team has read its
+//     slot it refills it with CTA row n + S and publishes n + S in the slot's
+//     sequence word (release store); the team that processes that row
+//     acquires the word before it waits on the mbarrier phase, which rules
+//     out waiting on a stale phase of a slot it did not drain itself. With
+//     S > teams, S - teams rows stay in flight while every team computes.
 //   * gamma is converted to fp32 once per CTA into shared memory.
-//   * Each team has `stages` shared-memory slots; a row of x and one of
-//     residual enter a slot by two cp.async.bulk copies (TMA engine, no
-//     multicast) that complete on the slot's mbarrier.
 //   * Thread t of a team owns the 16-byte vectors v = k*T + t, k < K, of a
 //     row. Phase 1: r = x + residual (fp32), residual_out written once,
 //     sum(r*r) in fp64, w = r*gamma kept in registers, per-group absmax by
 //     xor-shuffles over the GL = G/8 lanes of a group. One team barrier
-//     reduces sum(r*r); right after it the slot is refilled with the team's
-//     next row, so the copy overlaps phase 2. Phase 2: norm = w*inv_rms,
+//     reduces sum(r*r) and frees the slot. Phase 2: norm = w*inv_rms,
 //     scale, q (int8 truncation or e4m3 RNE with saturation).
 //   * sum(r*r) is accumulated in fp64 (exact squares of fp32 values, error
 //     ~1e-16 relative) and rounded to fp32 once, so inv_rms does not depend
@@ -31,7 +35,7 @@
 //     flips a group-maximum element (which sits on ±QMAX mathematically)
 //     between two codes, on ~1/(2G) of all elements.
 //   * Every device-side wait is bounded; a wait that runs out sets the
-//     caller's status word, and the team drains its copies and returns.
+//     caller's status word, and the CTA drains its copies and returns.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -50,9 +54,9 @@ constexpr int kMaxTeamWarps = kMaxTeamThreads / 32;
 // Largest D: gamma (4D bytes) and one slot (4D bytes for 2-byte inputs) must
 // fit the 227 KB of shared memory a CTA may use.
 constexpr int64_t kMaxHidden = 16384;
-constexpr int kMaxStages = 4;
+constexpr int kMaxStages = 8;           // ring slots per CTA
 constexpr int kMaxTeams = 15;         // named barriers 1..15
-constexpr uint32_t kSpinLimit = 1u << 26;  // bounded mbarrier polls
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // bound of every device-side wait (2 s)
 
 struct Params {
   const uint8_t* x;
@@ -78,15 +82,16 @@ struct Params {
 
 // Shared-memory carve-up, identical on host and device.
 struct SmemLayout {
-  size_t gamma, stages, bars, red, total;
+  size_t gamma, stages, bars, seq, red, total;
 };
 __host__ __device__ inline SmemLayout smem_layout(int D, uint32_t row_bytes, int teams,
                                                   int stages) {
   SmemLayout L;
   L.gamma = 0;
   L.stages = (size_t)D * sizeof(float);                       // multiple of 32
-  L.bars = L.stages + (size_t)teams * stages * 2 * row_bytes;  // multiple of 32
-  L.red = L.bars + (size_t)teams * stages * sizeof(uint64_t);
+  L.bars = L.stages + (size_t)stages * 2 * row_bytes;         // multiple of 32
+  L.seq = L.bars + (size_t)stages * sizeof(uint64_t);
+  L.red = L.seq + (size_t)kMaxStages * sizeof(uint32_t);      // 8-byte aligned
   L.total = L.red + (size_t)teams * kMaxTeamWarps * sizeof(double);
   return L;
 }
@@ -113,11 +118,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait: true when the phase completed, false when the poll limit ran out.
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait: true when the phase completed, false after kWaitLimitNs.
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i)
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-  return false;
+    if ((i & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  }
 }
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t pol;
@@ -133,6 +146,25 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
       " [%0], [%1], %2, [%3], %4;" ::"r"(dst),
       "l"(src), "r"(bytes), "r"(bar), "l"(pol)
       : "memory");
+}
+// Release store / acquire load of a shared-memory word (slot sequence numbers).
+__device__ __forceinline__ void seq_release(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_u32(p)), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(p)) : "memory");
+  return v;
+}
+// Bounded wait for a slot's sequence word to reach `want`.
+__device__ __forceinline__ bool seq_wait_bounded(const uint32_t* p, uint32_t want) {
+  if (ld_acquire(p) == want) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (ld_acquire(p) == want) return true;
+    __nanosleep(64);
+    if ((i & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  }
 }
 // Named barrier over `count` threads.
 __device__ __forceinline__ void team_sync(uint32_t id, uint32_t count) {
@@ -245,9 +277,9 @@ __device__ __forceinline__ uint32_t i8(float v) {
 // Round a positive normal fp32 up to the next power of two (identity on
 // powers of two): clear the mantissa, bump the exponent if it was non-zero.
 __device__ __forceinline__ float pow2_ceil(float s) {
-  uint32_t b = __float_as_uint(s);
-  if (b & 0x007fffffu) b = (b & 0xff800000u) + 0x00800000u;
-  return __uint_as_float(b);
+  const uint32_t b = __float_as_uint(s);
+  const uint32_t up = (b + 0x007fffffu) & 0xff800000u;  // carries into the exponent iff mantissa != 0
+  return __uint_as_float(up);
 }
 
 // -------------------------------------------------------------------- kernel
@@ -256,70 +288,86 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_rows_kernel(const Para
   extern __shared__ __align__(128) uint8_t smem[];
   const SmemLayout L = smem_layout(p.D, p.row_bytes, p.teams, p.stages);
   const int T = p.team_threads;
+  const int TEAMS = p.teams;
   const int team = threadIdx.x / T;
   const int tt = threadIdx.x - team * T;
   const int lane = threadIdx.x & 31;
   const int twarp = tt >> 5;
-  const int S = p.stages;
+  const int S = p.stages;  // ring slots of the CTA, S >= TEAMS
   const uint32_t stage_bytes = 2u * p.row_bytes;
   const uint32_t bar_id = 1u + (uint32_t)team;
 
   const float4* sg = reinterpret_cast<const float4*>(smem + L.gamma);
-  uint8_t* my_stage0 = smem + L.stages + (size_t)team * S * stage_bytes;
-  uint64_t* my_bars = reinterpret_cast<uint64_t*>(smem + L.bars) + team * S;
+  uint8_t* ring = smem + L.stages;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint32_t* seq = reinterpret_cast<uint32_t*>(smem + L.seq);
   double* my_red = reinterpret_cast<double*>(smem + L.red) + team * kMaxTeamWarps;
 
-  const int64_t tg = (int64_t)blockIdx.x * p.teams + team;
-  const int64_t ntot = (int64_t)gridDim.x * p.teams;
-  const int64_t nrows = tg < p.M ? (p.M - 1 - tg) / ntot + 1 : 0;
+  // CTA-local row n is global row blockIdx.x + n*gridDim.x; it sits in ring
+  // slot n % S and is processed by team n % TEAMS.
+  const int64_t G = gridDim.x;
+  const int64_t nrows = blockIdx.x < p.M ? (p.M - 1 - blockIdx.x) / G + 1 : 0;
+  const uint64_t pol = policy_evict_first();
 
-  uint64_t pol = 0;
-  int64_t issued = 0;  // rows queued by this team (thread 0 of the team only)
-  if (tt == 0) {
-    pol = policy_evict_first();
-    for (int s = 0; s < S; ++s) mbar_init(smem_u32(&my_bars[s]), 1);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) mbar_init(smem_u32(&bars[s]), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    for (; issued < nrows && issued < S; ++issued) {
-      const int64_t row = tg + issued * ntot;
-      const uint32_t bar = smem_u32(&my_bars[issued]);
-      const uint32_t dst = smem_u32(my_stage0 + (size_t)issued * stage_bytes);
-      mbar_arrive_expect_tx(bar, stage_bytes);
-      bulk_load(dst, p.x + row * p.sx, p.row_bytes, bar, pol);
-      bulk_load(dst + p.row_bytes, p.res + row * p.sr, p.row_bytes, bar, pol);
+    for (int s = 0; s < S; ++s) {
+      seq[s] = (uint32_t)s;
+      if (s < nrows) {
+        const int64_t row = blockIdx.x + (int64_t)s * G;
+        const uint32_t bar = smem_u32(&bars[s]);
+        const uint32_t dst = smem_u32(ring + (size_t)s * stage_bytes);
+        mbar_arrive_expect_tx(bar, stage_bytes);
+        bulk_load(dst, p.x + row * p.sx, p.row_bytes, bar, pol);
+        bulk_load(dst + p.row_bytes, p.res + row * p.sr, p.row_bytes, bar, pol);
+      }
     }
   }
-  // gamma -> fp32 shared memory, once per CTA (overlaps the first copies).
+  // gamma -> fp32 shared memory, once per CTA (overlaps the first copies),
+  // in two planes (elements 0-3, then 4-7 of every vector) so that a warp's
+  // 16-byte reads of one plane are contiguous (no bank conflicts).
   for (int v = threadIdx.x; v < p.nvec; v += blockDim.x) {
     float g[8];
     load_gamma8(p.gamma, v, p.gamma_dtype, g);
-    float4* d = reinterpret_cast<float4*>(smem + L.gamma) + 2 * v;
-    d[0] = make_float4(g[0], g[1], g[2], g[3]);
-    d[1] = make_float4(g[4], g[5], g[6], g[7]);
+    float4* d = reinterpret_cast<float4*>(smem + L.gamma);
+    d[v] = make_float4(g[0], g[1], g[2], g[3]);
+    d[p.nvec + v] = make_float4(g[4], g[5], g[6], g[7]);
   }
   __syncthreads();
-  if (nrows == 0) return;
 
   const float qmax = E4M3 ? 448.0f : 127.0f;
   const int nvec = p.nvec;
   const int tw = T >> 5;
-  int64_t consumed = nrows;
-  bool aborted = false;
+  bool failed = false;
 
-  for (int64_t i = 0; i < nrows; ++i) {
-    const int s = (int)(i % S);
-    const uint32_t parity = (uint32_t)((i / S) & 1);
-    const bool ok = mbar_wait_bounded(smem_u32(&my_bars[s]), parity);
+  // This team's rows n = team, team + TEAMS, ...: slot s = n % S and the
+  // slot's fill count j = n / S are advanced incrementally.
+  int64_t n = team;
+  int s = team % S;
+  uint32_t j = (uint32_t)(team / S);
+  const int64_t step_rows = (int64_t)TEAMS * G;
+  uint8_t* rout_row = p.rout + (blockIdx.x + n * G) * p.sro;
+  uint8_t* nout_row = p.nout ? p.nout + (blockIdx.x + n * G) * p.sno : nullptr;
+  uint8_t* q_row = p.q + (blockIdx.x + n * G) * p.sq;
+  float* sc_row = p.scale + (blockIdx.x + n * G) * p.ss;
+  const int64_t d_ro = step_rows * p.sro, d_no = step_rows * p.sno;
+  const int64_t d_q = step_rows * p.sq, d_s = step_rows * p.ss;
+
+  for (; n < nrows; n += TEAMS) {
+    // Wait until the slot holds row n: first its sequence word (written
+    // with release semantics by the team that armed the slot, so the
+    // mbarrier phase below cannot be a stale one), then the copy itself.
+    bool ok = seq_wait_bounded(&seq[s], (uint32_t)n);
+    ok = ok && mbar_wait_bounded(smem_u32(&bars[s]), j & 1u);
     if (team_sync_or(bar_id, T, !ok)) {
       if (tt == 0 && p.status) atomicExch(p.status, (int)FARQ_ERR_DEVICE_TIMEOUT);
-      consumed = i;
-      aborted = true;
+      failed = true;
       break;
     }
-    const int64_t row = tg + i * ntot;
-    const uint8_t* sx = my_stage0 + (size_t)s * stage_bytes;
+    const uint8_t* sx = ring + (size_t)s * stage_bytes;
     const uint8_t* sr = sx + p.row_bytes;
-    uint8_t* rout_row = p.rout + row * p.sro;
 
     // ---- phase 1
     float w[K][8];
@@ -333,7 +381,7 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_rows_kernel(const Para
         float a[8], b[8];
         Unpack<Tin>::run(reinterpret_cast<const uint4*>(sx)[v], a);
         Unpack<Tin>::run(reinterpret_cast<const uint4*>(sr)[v], b);
-        const float4 g0 = sg[2 * v], g1 = sg[2 * v + 1];
+        const float4 g0 = sg[v], g1 = sg[nvec + v];
         const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
@@ -360,33 +408,30 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_rows_kernel(const Para
     if (lane == 0) my_red[twarp] = ss;
     team_sync(bar_id, T);
 
-    // The slot is no longer read: queue the team's row that uses it next.
-    if (tt == 0 && issued < nrows) {
-      const int64_t nrow = tg + issued * ntot;
-      const uint32_t bar = smem_u32(&my_bars[s]);
-      const uint32_t dst = smem_u32(my_stage0 + (size_t)s * stage_bytes);
+    // The slot is no longer read: refill it with CTA row n + S.
+    if (tt == 0 && n + S < nrows) {
+      const int64_t row = blockIdx.x + (n + S) * G;
+      const uint32_t bar = smem_u32(&bars[s]);
+      const uint32_t dst = smem_u32(ring + (size_t)s * stage_bytes);
       mbar_arrive_expect_tx(bar, stage_bytes);
-      bulk_load(dst, p.x + nrow * p.sx, p.row_bytes, bar, pol);
-      bulk_load(dst + p.row_bytes, p.res + nrow * p.sr, p.row_bytes, bar, pol);
-      ++issued;
+      bulk_load(dst, p.x + row * p.sx, p.row_bytes, bar, pol);
+      bulk_load(dst + p.row_bytes, p.res + row * p.sr, p.row_bytes, bar, pol);
+      seq_release(&seq[s], (uint32_t)(n + S));
     }
 
     double total = 0.0;
-    for (int j = 0; j < tw; ++j) total += my_red[j];
+    for (int q = 0; q < tw; ++q) total += my_red[q];
     const float inv_rms =
         __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(__double2float_rn(total), (float)p.D), p.eps)));
     const float step = __fdiv_rn(inv_rms, qmax);
 
     // ---- phase 2
-    uint8_t* nout_row = p.nout ? p.nout + row * p.sno : nullptr;
-    uint8_t* q_row = p.q + row * p.sq;
-    float* sc_row = p.scale + row * p.ss;
 #pragma unroll
     for (int k = 0; k < K; ++k) {
       const int v = k * T + tt;
       if (v < nvec) {
         float sc = fmaxf(gmax[k] * step, 1.0e-12f);
-        if (p.ue8m0) sc = pow2_ceil(sc);
+        sc = p.ue8m0 ? pow2_ceil(sc) : sc;
         const float isc = __frcp_rn(sc);
         float nrm[8];
 #pragma unroll
@@ -406,13 +451,25 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_rows_kernel(const Para
         if ((lane & (GL - 1)) == 0) st_cs_f32(sc_row + v / GL, sc);
       }
     }
+    rout_row += d_ro;
+    if (nout_row) nout_row += d_no;
+    q_row += d_q;
+    sc_row += d_s;
+    s += TEAMS;
+    if (s >= S) {
+      s -= S;
+      ++j;
+    }
   }
 
-  // Abort path: no bulk copy may still target this team's shared memory
-  // when the CTA exits. Copies for rows [consumed, issued) may be in flight.
-  if (aborted && tt == 0) {
-    for (int64_t j = consumed; j < issued; ++j)
-      (void)mbar_wait_bounded(smem_u32(&my_bars[j % S]), (uint32_t)((j / S) & 1));
+  // No bulk copy may still target this CTA's shared memory when it exits:
+  // after a failed wait, drain every slot's last armed fill (bounded).
+  if (__syncthreads_or(failed) && threadIdx.x == 0) {
+    for (int t = 0; t < S; ++t) {
+      const uint32_t last = ld_acquire(&seq[t]);
+      if ((int64_t)last < nrows)
+        (void)mbar_wait_bounded(smem_u32(&bars[t]), (last / (uint32_t)S) & 1u);
+    }
   }
 }
 

@@ -96,7 +96,7 @@ typedef struct farq_args {
     float    eps;
     int32_t  tune_ctas_per_sm;     /* 0 = auto (1)                          */
     int32_t  tune_teams_per_cta;   /* 0 = auto; upper bound on row teams    */
-    int32_t  tune_stages;          /* 0 = auto; shared-memory slots per team */
+    int32_t  tune_stages;          /* 0 = auto; ring slots per CTA (>= teams) */
     int32_t  tune_vec_per_thread;  /* 0 = auto; 1..8 16-byte vectors        */
     int32_t  reserved0;            /* must be 0                             */
     const void* x;                 /* [M, D]                                */
