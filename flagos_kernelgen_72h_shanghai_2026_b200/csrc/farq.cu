@@ -314,7 +314,9 @@ int farq_launch(const farq_args_t* a, void* stream) {
   p.rout_dtype = a->residual_out_dtype;
   p.nout_dtype = a->norm_out_dtype;
   p.ue8m0 = (a->flags & FARQ_FLAG_UE8M0) ? 1 : 0;
+  p.force_timeout = (a->flags & FARQ_FLAG_TEST_FORCE_TIMEOUT) ? 1 : 0;
   p.eps = a->eps;
+  p.wait_limit_ns = p.force_timeout ? kTestWaitLimitNs : kWaitLimitNs;
 
   void* kargs[] = {&p};
   if (cudaLaunchKernel(reinterpret_cast<const void*>(ks.fn), dim3(pl.grid),

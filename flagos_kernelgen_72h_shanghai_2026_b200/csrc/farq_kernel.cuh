@@ -56,7 +56,8 @@ constexpr int kMaxTeamWarps = kMaxTeamThreads / 32;
 constexpr int64_t kMaxHidden = 16384;
 constexpr int kMaxStages = 8;           // ring slots per CTA
 constexpr int kMaxTeams = 15;         // named barriers 1..15
-constexpr uint64_t kWaitLimitNs = 2000000000ull;  // bound of every device-side wait (2 s)
+constexpr uint64_t kWaitLimitNs = 2000000000ull;   // default bound of device waits (2 s)
+constexpr uint64_t kTestWaitLimitNs = 1000000ull;  // bound under the test-only forced timeout
 
 struct Params {
   const uint8_t* x;
@@ -77,7 +78,9 @@ struct Params {
   uint32_t row_bytes;  // D * sizeof(x element)
   int32_t gamma_dtype, rout_dtype, nout_dtype;
   int32_t ue8m0;
+  int32_t force_timeout;  // test only: team 0 waits for a sequence value nobody writes
   float eps;
+  uint64_t wait_limit_ns; // bound of every device-side wait
 };
 
 // Shared-memory carve-up, identical on host and device.
@@ -123,13 +126,13 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// Bounded wait: true when the phase completed, false after kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+// Bounded wait: true when the phase completed, false after limit_ns.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    if ((i & 255u) == 0 && globaltimer_ns() - t0 > limit_ns) return false;
   }
 }
 __device__ __forceinline__ uint64_t policy_evict_first() {
@@ -157,13 +160,13 @@ __device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
   return v;
 }
 // Bounded wait for a slot's sequence word to reach `want`.
-__device__ __forceinline__ bool seq_wait_bounded(const uint32_t* p, uint32_t want) {
+__device__ __forceinline__ bool seq_wait_bounded(const uint32_t* p, uint32_t want, uint64_t limit_ns) {
   if (ld_acquire(p) == want) return true;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (ld_acquire(p) == want) return true;
     __nanosleep(64);
-    if ((i & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) return false;
+    if ((i & 63u) == 0 && globaltimer_ns() - t0 > limit_ns) return false;
   }
 }
 // Named barrier over `count` threads.
@@ -359,8 +362,9 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_rows_kernel(const Para
     // Wait until the slot holds row n: first its sequence word (written
     // with release semantics by the team that armed the slot, so the
     // mbarrier phase below cannot be a stale one), then the copy itself.
-    bool ok = seq_wait_bounded(&seq[s], (uint32_t)n);
-    ok = ok && mbar_wait_bounded(smem_u32(&bars[s]), j & 1u);
+    const uint32_t want = (p.force_timeout && team == 0) ? 0xffffffffu : (uint32_t)n;
+    bool ok = seq_wait_bounded(&seq[s], want, p.wait_limit_ns);
+    ok = ok && mbar_wait_bounded(smem_u32(&bars[s]), j & 1u, p.wait_limit_ns);
     if (team_sync_or(bar_id, T, !ok)) {
       if (tt == 0 && p.status) atomicExch(p.status, (int)FARQ_ERR_DEVICE_TIMEOUT);
       failed = true;
@@ -468,7 +472,7 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_rows_kernel(const Para
     for (int t = 0; t < S; ++t) {
       const uint32_t last = ld_acquire(&seq[t]);
       if ((int64_t)last < nrows)
-        (void)mbar_wait_bounded(smem_u32(&bars[t]), (last / (uint32_t)S) & 1u);
+        (void)mbar_wait_bounded(smem_u32(&bars[t]), (last / (uint32_t)S) & 1u, p.wait_limit_ns);
     }
   }
 }

@@ -79,6 +79,7 @@ def fused_add_rmsnorm_group_quant(
     _tune_stages: int = 0,
     _tune_vec_per_thread: int = 0,
     _status: torch.Tensor | None = None,
+    _test_force_timeout: bool = False,
 ):
     """residual_out = x + residual; norm = RMSNorm(residual_out) * gamma;
     per-group quantisation of norm into (x_q, x_scale). Asynchronous on the
@@ -142,7 +143,8 @@ def fused_add_rmsnorm_group_quant(
     a.residual_out_dtype = ro_dt
     a.norm_out_dtype = no_dt
     a.q_dtype = q_dt
-    a.flags = _lib.FLAG_UE8M0 if ue8m0 else 0
+    a.flags = (_lib.FLAG_UE8M0 if ue8m0 else 0) | (
+        _lib.FLAG_TEST_FORCE_TIMEOUT if _test_force_timeout else 0)
     a.group_size = group_size
     a.M = M
     a.D = D

@@ -51,7 +51,12 @@ enum farq_dtype {
 
 /* flags bits. */
 enum farq_flags {
-    FARQ_FLAG_UE8M0 = 1 /* round every scale up to a power of two (E4M3 only) */
+    FARQ_FLAG_UE8M0 = 1,  /* round every scale up to a power of two            */
+    /* Test only: the first row team of every CTA waits for a slot sequence
+     * value that is never written, with every device wait limited to 1 ms,
+     * so the bounded-wait path (status word, drained copies, clean exit) can
+     * be exercised without a GPU fault. Rows of that team are not written. */
+    FARQ_FLAG_TEST_FORCE_TIMEOUT = 1 << 30
 };
 
 /* Status codes returned by every entry point. Never a device trap. */

@@ -280,6 +280,27 @@ def test_status_word_stays_zero(cuda_dev):
     assert int(status.item()) == 0
 
 
+def test_bounded_wait_times_out_into_status_word(cuda_dev):
+    """A device wait that nothing satisfies (test-only flag, 1 ms limit)
+    returns through the status word; the context stays usable."""
+    w = Workload("to", 1184, 4096, seed=31)
+    x, r, g = make_inputs(w, device="cuda")
+    ro = torch.empty_like(x)
+    q = torch.empty(w.M, w.D, dtype=torch.float8_e4m3fn, device="cuda")
+    s = torch.empty(w.M, w.groups, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    fused_add_rmsnorm_group_quant(x, r, g, ro, None, q, s, w.eps, 128, _status=status,
+                                  _test_force_timeout=True)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 9  # FARQ_ERR_DEVICE_TIMEOUT
+    status.zero_()
+    fused_add_rmsnorm_group_quant(x, r, g, ro, None, q, s, w.eps, 128, _status=status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    got = dict(residual_out=ro.cpu(), x_q=q.cpu(), x_scale=s.cpu())
+    check_outputs(got, ref_dict(x.cpu(), r.cpu(), g.cpu(), w.eps, 128, "e4m3"), "e4m3")
+
+
 def test_errors_raise(cuda_dev):
     dev = cuda_dev
     x = torch.zeros(4, 1000, dtype=torch.bfloat16, device=dev)
