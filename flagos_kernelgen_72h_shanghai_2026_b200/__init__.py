@@ -6,6 +6,7 @@ sinpeyw/flagos-kernelgen-72h-shanghai-2026
 signature, destination passing, same returned tensor objects. The device
 work is one hand-written sm_100a kernel in libfarq.so (C ABI: include/farq.h).
 """
+from .offload import fused_add_rmsnorm_group_quant_host  # noqa: F401
 from .task01 import fused_add_rmsnorm_group_quant, launch_plan  # noqa: F401
 
-__all__ = ["fused_add_rmsnorm_group_quant", "launch_plan"]
+__all__ = ["fused_add_rmsnorm_group_quant", "fused_add_rmsnorm_group_quant_host", "launch_plan"]

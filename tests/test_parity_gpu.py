@@ -301,6 +301,28 @@ def test_bounded_wait_times_out_into_status_word(cuda_dev):
     check_outputs(got, ref_dict(x.cpu(), r.cpu(), g.cpu(), w.eps, 128, "e4m3"), "e4m3")
 
 
+@pytest.mark.parametrize("chunk", [64, 500, 4096])
+def test_host_buffer_entry_matches_device_entry(cuda_dev, chunk):
+    from flagos_kernelgen_72h_shanghai_2026_b200 import fused_add_rmsnorm_group_quant_host
+    w = Workload("h", 1300, 7168, res_std=2.0, seed=37)
+    x, r, g = make_inputs(w)
+    dev = run_gpu(x, r, g, w.eps, 128, torch.float8_e4m3fn, cuda_dev)
+    hx, hr = x.pin_memory(), r.pin_memory()
+    ro = torch.empty_like(hx).pin_memory()
+    no = torch.empty(w.M, w.D, dtype=torch.bfloat16).pin_memory()
+    q = torch.empty(w.M, w.D, dtype=torch.float8_e4m3fn).pin_memory()
+    s = torch.empty(w.M, w.groups).pin_memory()
+    for _ in range(2):  # second call reuses the cached staging pipeline
+        out = fused_add_rmsnorm_group_quant_host(hx, hr, g, ro, no, q, s, w.eps, 128,
+                                                 device=cuda_dev, chunk_rows=chunk)
+        torch.cuda.current_stream().synchronize()
+        assert out[0] is ro and out[2] is q
+        got = dict(residual_out=ro, norm_out=no, x_q=q, x_scale=s)
+        for k in got:
+            assert torch.equal(got[k].view(torch.uint8), dev[k].view(torch.uint8)), k
+        ro.zero_(); q.view(torch.uint8).zero_(); s.zero_()
+
+
 def test_errors_raise(cuda_dev):
     dev = cuda_dev
     x = torch.zeros(4, 1000, dtype=torch.bfloat16, device=dev)
