@@ -318,11 +318,20 @@ int farq_launch(const farq_args_t* a, void* stream) {
   p.eps = a->eps;
   p.wait_limit_ns = p.force_timeout ? kTestWaitLimitNs : kWaitLimitNs;
 
-  void* kargs[] = {&p};
-  if (cudaLaunchKernel(reinterpret_cast<const void*>(ks.fn), dim3(pl.grid),
-                       dim3(pl.team_threads * pl.teams), kargs, pl.smem,
-                       static_cast<cudaStream_t>(stream)) != cudaSuccess)
-    return FARQ_ERR_CUDA;
+  // Programmatic stream serialisation lets this launch overlap the tail of
+  // the previous kernel in the stream; the kernel waits for it
+  // (griddepcontrol.wait) before its first global-memory access.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.grid);
+  cfg.blockDim = dim3(pl.team_threads * pl.teams);
+  cfg.dynamicSmemBytes = pl.smem;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, ks.fn, p) != cudaSuccess) return FARQ_ERR_CUDA;
   return FARQ_OK;
 }
 

@@ -34,6 +34,9 @@
 //     on the summation order. With fp32 accumulation every ulp of inv_rms
 //     flips a group-maximum element (which sits on ±QMAX mathematically)
 //     between two codes, on ~1/(2G) of all elements.
+//   * Launched with programmatic stream serialisation: the next call's CTAs
+//     launch and set up while this one drains, and wait (griddepcontrol)
+//     before their first global-memory access.
 //   * Every device-side wait is bounded; a wait that runs out sets the
 //     caller's status word, and the CTA drains its copies and returns.
 #pragma once
@@ -311,6 +314,12 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_rows_kernel(const Para
   const int64_t G = gridDim.x;
   const int64_t nrows = blockIdx.x < p.M ? (p.M - 1 - blockIdx.x) / G + 1 : 0;
   const uint64_t pol = policy_evict_first();
+  // Programmatic dependent launch: this grid may have been started while the
+  // previous kernel in the stream was still draining. Wait for it to finish
+  // (and its writes to be visible) before touching global memory, and let the
+  // next launch begin its own set-up as early as possible.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) mbar_init(smem_u32(&bars[s]), 1);
