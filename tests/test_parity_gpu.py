@@ -350,3 +350,4 @@ def test_launch_plan_reports_persistent_grid(cuda_dev):
     assert p["grid"] == sms and p["teams"] >= 1 and p["stages"] >= 1
     small = launch_plan(5, 7168)
     assert small["grid"] == 5 and small["teams"] == 1
+    assert small["team_threads"] == 448 and small["vec_per_thread"] == 2  # widest team
