@@ -268,9 +268,15 @@ int farq_launch(const farq_args_t* a, void* stream) {
   const int64_t sro = a->residual_out_row_stride ? a->residual_out_row_stride : D;
   const int64_t sno = a->norm_out_row_stride ? a->norm_out_row_stride : D;
   const int64_t sq = a->x_q_row_stride ? a->x_q_row_stride : D;
-  const int64_t ss = a->x_scale_row_stride ? a->x_scale_row_stride : D / G;
-  if (sx < D || sr < D || sro < D || sq < D || ss < D / G || (a->norm_out && sno < D))
+  // x_scale: [M, D/G] row-major (row stride >= D/G), or with
+  // FARQ_FLAG_SCALE_COLUMN_MAJOR [D/G, ld] (ld = x_scale_row_stride >= M).
+  const bool scale_cm = (a->flags & FARQ_FLAG_SCALE_COLUMN_MAJOR) != 0;
+  const int64_t sld = a->x_scale_row_stride ? a->x_scale_row_stride : (scale_cm ? M : D / G);
+  if (sx < D || sr < D || sro < D || sq < D || (a->norm_out && sno < D) ||
+      sld < (scale_cm ? M : D / G))
     return FARQ_ERR_BAD_SHAPE;
+  const int64_t ss = scale_cm ? 1 : sld;    // floats between consecutive rows' scales
+  const int64_t sgs = scale_cm ? sld : 1;   // floats between consecutive groups' scales
   // 16-byte rows for the bulk copies and vector stores; 8-byte q rows.
   if (!aligned(a->x, 16) || !aligned(a->residual, 16) || !aligned(a->residual_out, 16) ||
       !aligned(a->gamma, 16) || (a->norm_out && !aligned(a->norm_out, 16)) ||
@@ -310,6 +316,7 @@ int farq_launch(const farq_args_t* a, void* stream) {
   p.sno = a->norm_out ? sno * nos : 0;
   p.sq = sq;
   p.ss = ss;
+  p.sgs = sgs;
   p.D = (int32_t)D;
   p.nvec = (int32_t)(D / 8);
   p.team_threads = pl.team_threads;

@@ -73,6 +73,7 @@ struct Params {
   int32_t* status;   // may be null
   int64_t M;
   int64_t sx, sr, sro, sno, sq, ss;  // row strides in bytes (ss: in floats)
+  int64_t sgs;                       // x_scale group stride in floats (1: row-major)
   int32_t D;
   int32_t nvec;      // D / 8
   int32_t team_threads;
@@ -461,7 +462,7 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_rows_kernel(const Para
                (i8(nrm[7] * isc) << 24);
         }
         st_cs_v2(q_row + 8 * (int64_t)v, lo, hi);
-        if ((lane & (GL - 1)) == 0) st_cs_f32(sc_row + v / GL, sc);
+        if ((lane & (GL - 1)) == 0) st_cs_f32(sc_row + (v / GL) * p.sgs, sc);
       }
     }
     rout_row += d_ro;

@@ -15,7 +15,9 @@ callers see the reference contract:
     gives scale over 448 and a saturating round-to-nearest-even cast.
   * ``norm_out`` may be ``None`` or empty: the normalised tensor is skipped.
   * ``ue8m0=True`` rounds every scale up to a power of two.
-  * Row-strided (inner-contiguous) views are accepted.
+  * Row-strided (inner-contiguous) views are accepted, and ``x_scale`` may be
+    a column-major view (``buf[:, :M].t()`` of a ``[D/G, ld]`` buffer), the
+    scale layout blockwise-FP8 GEMMs read.
 
 Errors: ``TypeError`` for a non-CUDA tensor or a dtype the kernel does not
 take, ``ValueError`` for shapes, group sizes and alignment, ``RuntimeError``
@@ -131,7 +133,11 @@ def fused_add_rmsnorm_group_quant(
     sr = _row_stride("residual", residual, M, D)
     sro = _row_stride("residual_out", residual_out, M, D)
     sq = _row_stride("x_q", x_q, M, D)
-    ss = _row_stride("x_scale", x_scale, M, groups)
+    # x_scale may be a column-major ("MN-major") view, e.g. buf[:, :M].t() of a
+    # [groups, ld] buffer as blockwise-FP8 GEMMs take it.
+    scale_cm = (x_scale.dim() == 2 and tuple(x_scale.shape) == (M, groups) and M > 1
+                and x_scale.stride(0) == 1 and x_scale.stride(1) >= M and groups > 1)
+    ss = x_scale.stride(1) if scale_cm else _row_stride("x_scale", x_scale, M, groups)
     sno = _row_stride("norm_out", norm_out, M, D) if write_norm else 0
     if M == 0:
         return residual_out, norm_out, x_q, x_scale
@@ -144,6 +150,7 @@ def fused_add_rmsnorm_group_quant(
     a.norm_out_dtype = no_dt
     a.q_dtype = q_dt
     a.flags = (_lib.FLAG_UE8M0 if ue8m0 else 0) | (
+        _lib.FLAG_SCALE_COLUMN_MAJOR if scale_cm else 0) | (
         _lib.FLAG_TEST_FORCE_TIMEOUT if _test_force_timeout else 0)
     a.group_size = group_size
     a.M = M

@@ -52,6 +52,11 @@ enum farq_dtype {
 /* flags bits. */
 enum farq_flags {
     FARQ_FLAG_UE8M0 = 1,  /* round every scale up to a power of two            */
+    /* x_scale is column-major [D/G, ld] ("MN-major", the layout blockwise-FP8
+     * GEMMs read scales in): scale of (row m, group g) at x_scale[g*ld + m],
+     * ld = x_scale_row_stride (0 = M). No reference counterpart: the reference
+     * writes [M, D/G] row-major only (task01…py:1112). */
+    FARQ_FLAG_SCALE_COLUMN_MAJOR = 2,
     /* Test only: the first row team of every CTA waits for a slot sequence
      * value that is never written, with every device wait limited to 1 ms,
      * so the bounded-wait path (status word, drained copies, clean exit) can

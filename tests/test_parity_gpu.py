@@ -323,6 +323,24 @@ def test_host_buffer_entry_matches_device_entry(cuda_dev, chunk):
         ro.zero_(); q.view(torch.uint8).zero_(); s.zero_()
 
 
+def test_column_major_scales(cuda_dev):
+    """x_scale as a transposed [groups, ld] buffer (the layout blockwise-FP8
+    GEMMs read); every other output identical to the row-major call."""
+    w = Workload("cm", 300, 7168, seed=41)
+    x, r, g = make_inputs(w)
+    base = run_gpu(x, r, g, w.eps, 128, torch.float8_e4m3fn, cuda_dev)
+    ld = 304  # M rounded up to a multiple of 16
+    buf = torch.full((w.groups, ld), -1.0, device="cuda")
+    s_cm = buf[:, :w.M].t()
+    ro = torch.empty(w.M, w.D, dtype=torch.bfloat16, device="cuda")
+    q = torch.empty(w.M, w.D, dtype=torch.float8_e4m3fn, device="cuda")
+    fused_add_rmsnorm_group_quant(x.cuda(), r.cuda(), g.cuda(), ro, None, q, s_cm, w.eps, 128)
+    torch.cuda.synchronize()
+    assert torch.equal(s_cm.cpu(), base["x_scale"])
+    assert torch.all(buf[:, w.M:] == -1.0)  # padding columns untouched
+    assert torch.equal(q.cpu().view(torch.uint8), base["x_q"].view(torch.uint8))
+
+
 def test_errors_raise(cuda_dev):
     dev = cuda_dev
     x = torch.zeros(4, 1000, dtype=torch.bfloat16, device=dev)
