@@ -101,6 +101,8 @@ def load(path: Path | str | None = None) -> ctypes.CDLL:
                                   ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
                                   ctypes.POINTER(ctypes.c_int64)]
         lib.farq_plan.restype = ctypes.c_int
+        lib.farq_ar_launch.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+        lib.farq_ar_launch.restype = ctypes.c_int
         v = lib.farq_abi_version()
         if v != ABI_VERSION:
             raise RuntimeError(f"libfarq.so ABI version {v} != expected {ABI_VERSION}; rebuild it")

@@ -13,6 +13,7 @@
 
 #include "farq.h"
 #include "farq_kernel.cuh"
+#include "farq_ar_kernel.cuh"
 
 namespace farq {
 
@@ -345,6 +346,98 @@ int farq_launch(const farq_args_t* a, void* stream) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, ks.fn, p) != cudaSuccess) return FARQ_ERR_CUDA;
+  return FARQ_OK;
+}
+
+int farq_ar_launch(const farq_ar_args_t* a, void* stream) {
+  if (!a) return FARQ_ERR_NULL_POINTER;
+  if (a->struct_size != sizeof(farq_ar_args_t)) return FARQ_ERR_BAD_ARGS_SIZE;
+  const int64_t M = a->M, D = a->D;
+  const int G = a->group_size, W = a->world;
+  int st = check_shape(M, D, G);
+  if (st != FARQ_OK) return st;
+  if (W < 1 || W > kMaxWorld || a->rank < 0 || a->rank >= W) return FARQ_ERR_BAD_SHAPE;
+  if (a->x_dtype != FARQ_DTYPE_BF16 && a->x_dtype != FARQ_DTYPE_FP16) return FARQ_ERR_BAD_DTYPE;
+  if (!is_float_out(a->gamma_dtype)) return FARQ_ERR_BAD_DTYPE;
+  if (a->q_dtype != FARQ_DTYPE_INT8 && a->q_dtype != FARQ_DTYPE_E4M3) return FARQ_ERR_BAD_DTYPE;
+  const bool with_norm = a->norm_out[0] != nullptr;
+  if (with_norm && !is_float_out(a->norm_out_dtype)) return FARQ_ERR_BAD_DTYPE;
+  if (M == 0) return FARQ_OK;
+  if (!a->residual || !a->gamma) return FARQ_ERR_NULL_POINTER;
+  if (!aligned(a->residual, 16) || !aligned(a->gamma, 16)) return FARQ_ERR_ALIGNMENT;
+  for (int k = 0; k < W; ++k) {
+    if (!a->partial[k] || !a->residual_out[k] || !a->x_q[k] || !a->x_scale[k] || !a->signal[k] ||
+        (with_norm && !a->norm_out[k]))
+      return FARQ_ERR_NULL_POINTER;
+    if (!aligned(a->partial[k], 16) || !aligned(a->residual_out[k], 16) || !aligned(a->x_q[k], 8) ||
+        !aligned(a->x_scale[k], 4) || !aligned(a->signal[k], 4) ||
+        (with_norm && !aligned(a->norm_out[k], 16)))
+      return FARQ_ERR_ALIGNMENT;
+  }
+  int dev, sms, optin;
+  if (device_info(&dev, &sms, &optin) != cudaSuccess) return FARQ_ERR_CUDA;
+  const int xs = dtype_size(a->x_dtype);
+  const uint32_t row_bytes = (uint32_t)(D * xs);
+  int K, T;
+  st = pick_k(D / 8, 0, false, &K, &T);
+  if (st != FARQ_OK) return st;
+  // Slots of (W + 1) rows next to gamma, as many as fit (at most kMaxStages).
+  int S = kMaxStages;
+  const int64_t cap = (int64_t)optin < kSmemPerSm - kSmemReservedPerCta ? optin
+                                                                         : kSmemPerSm - kSmemReservedPerCta;
+  while (S > 0 && (int64_t)ar_layout((int)D, row_bytes, W, S).total > cap) --S;
+  if (S < 1) return FARQ_ERR_UNSUPPORTED;
+  // The grid must be the same on every rank (CTA b meets CTA b): derive it
+  // from the largest slab, ceil(M / W), not from this rank's slab.
+  int64_t grid = (M + W - 1) / W;
+  if (grid > sms) grid = sms;
+  if (grid > kMaxArCtas) grid = kMaxArCtas;
+  if (grid < 1) grid = 1;
+  const int gl = ilog2(G / 8);
+  ArKernelFn fn;
+  const bool e4m3 = a->q_dtype == FARQ_DTYPE_E4M3;
+  if (a->x_dtype == FARQ_DTYPE_BF16)
+    fn = e4m3 ? ar_kernel_bf16_e4m3(K, gl) : ar_kernel_bf16_int8(K, gl);
+  else
+    fn = e4m3 ? ar_kernel_fp16_e4m3(K, gl) : ar_kernel_fp16_int8(K, gl);
+  const size_t smem = ar_layout((int)D, row_bytes, W, S).total;
+  if (cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return FARQ_ERR_CUDA;
+
+  ArParams p = {};
+  for (int k = 0; k < W; ++k) {
+    p.part[k] = static_cast<const uint8_t*>(a->partial[k]);
+    p.rout[k] = static_cast<uint8_t*>(a->residual_out[k]);
+    p.nout[k] = with_norm ? static_cast<uint8_t*>(a->norm_out[k]) : nullptr;
+    p.q[k] = static_cast<uint8_t*>(a->x_q[k]);
+    p.scale[k] = a->x_scale[k];
+    p.signal[k] = a->signal[k];
+  }
+  p.res = static_cast<const uint8_t*>(a->residual);
+  p.gamma = a->gamma;
+  p.status = a->status;
+  // This rank's slab: equal slabs, the M % W remainder one row each to the last ranks.
+  const int64_t base = M / W, rem = M % W;
+  p.row_begin = a->rank * base + (a->rank > W - rem ? a->rank - (W - rem) : 0);
+  p.row_end = p.row_begin + base + (a->rank >= W - rem ? 1 : 0);
+  p.D = (int32_t)D;
+  p.nvec = (int32_t)(D / 8);
+  p.team_threads = T;
+  p.stages = S;
+  p.world = W;
+  p.rank = a->rank;
+  p.row_bytes = row_bytes;
+  p.gamma_dtype = a->gamma_dtype;
+  p.nout_dtype = a->norm_out_dtype;
+  p.ue8m0 = (a->flags & FARQ_FLAG_UE8M0) ? 1 : 0;
+  p.epoch = a->epoch;
+  p.eps = a->eps;
+  p.wait_limit_ns = kWaitLimitNs;
+  void* kargs[] = {&p};
+  if (cudaLaunchKernel(reinterpret_cast<const void*>(fn), dim3((unsigned)grid), dim3(T), kargs,
+                       smem, static_cast<cudaStream_t>(stream)) != cudaSuccess)
+    return FARQ_ERR_CUDA;
   return FARQ_OK;
 }
 

@@ -1,0 +1,329 @@
+// farq_ar_kernel.cuh — tensor-parallel variant: all-reduce of W partial
+// activations fused with residual add + RMSNorm + per-token group
+// quantisation, over NVLink peer memory (C ABI: farq_ar_launch, include/farq.h).
+//
+// Where it sits: in tensor-parallel inference the layer before the norm is a
+// row-parallel GEMM, so every rank holds a partial sum P_k [M, D] of x. The
+// reference operator (src/task01_fused_add_rmsnorm_group_quant.py:1731) runs
+// after an all-reduce has produced x on every rank; this kernel does both:
+//
+//   x        = round_to_input_dtype( sum_k fp32(P_k) )   (ranks k = 0..W-1 in order)
+//   then the reference per-row math on x and residual, with every output row
+//   written to all W ranks (the outputs are replicated, as after an all-reduce).
+//
+// Execution:
+//   * Rank r owns the contiguous row slab [row_begin, row_end); CTA b of rank r
+//     processes slab rows b, b + grid, ... One row team of T threads per CTA.
+//   * A ring of S shared-memory slots holds, per row, the W partial rows
+//     (read from each rank's memory by cp.async.bulk — unicast TMA copies,
+//     never multicast) and the local residual row, completing on the slot's
+//     mbarrier. The team refills a slot with its row S ahead right after the
+//     slot has been read.
+//   * Outputs are written with plain stores to each rank's buffer (peer
+//     pointers over NVLink, including this rank's own).
+//   * Two cross-rank barriers per CTA, on epoch flags in every rank's signal
+//     buffer: at the start (every rank's partial is complete and every rank has
+//     finished with the previous contents of its output buffers) and at the end
+//     (every peer's writes into this rank's outputs are visible before this
+//     kernel completes). CTA b of rank r meets CTA b of every other rank; the
+//     grid is identical on all ranks. Every wait is bounded in time; a wait
+//     that runs out sets the status word and the CTA returns.
+#pragma once
+
+#include <type_traits>
+
+#include "farq_kernel.cuh"
+
+namespace farq {
+
+constexpr int kMaxWorld = 8;
+constexpr int kMaxArCtas = 1024;  // signal-buffer slots per phase
+
+struct ArParams {
+  const uint8_t* part[kMaxWorld];  // partial activations, one per rank
+  uint8_t* rout[kMaxWorld];
+  uint8_t* nout[kMaxWorld];        // all null when norm_out is not written
+  uint8_t* q[kMaxWorld];
+  float* scale[kMaxWorld];
+  uint32_t* signal[kMaxWorld];     // each rank's signal buffer
+  const uint8_t* res;              // local residual
+  const void* gamma;
+  int32_t* status;
+  int64_t row_begin, row_end;      // this rank's slab
+  int32_t D, nvec, team_threads, stages, world, rank;
+  uint32_t row_bytes;              // D * sizeof(x element)
+  int32_t gamma_dtype, nout_dtype, ue8m0;
+  uint32_t epoch;
+  float eps;
+  uint64_t wait_limit_ns;
+};
+
+// Shared memory: gamma (fp32, two planes) | S slots of (W + 1) rows |
+// S mbarriers | reduction words.
+struct ArLayout {
+  size_t gamma, slots, bars, red, total;
+};
+__host__ __device__ inline ArLayout ar_layout(int D, uint32_t row_bytes, int world, int stages) {
+  ArLayout L;
+  L.gamma = 0;
+  L.slots = (size_t)D * sizeof(float);
+  L.bars = L.slots + (size_t)stages * (world + 1) * row_bytes;
+  L.red = L.bars + (size_t)stages * sizeof(uint64_t);
+  L.total = L.red + (size_t)kMaxTeamWarps * sizeof(double);
+  return L;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Cross-rank barrier of CTA blockIdx.x for `phase`: signal every rank, then
+// wait (bounded) until every rank has signalled this CTA. Returns false when
+// the wait ran out. Called by one thread.
+__device__ __forceinline__ bool ar_barrier(const ArParams& p, int phase) {
+  const size_t base = ((size_t)phase * kMaxArCtas + blockIdx.x) * kMaxWorld;
+  for (int k = 0; k < p.world; ++k) st_release_sys(p.signal[k] + base + p.rank, p.epoch);
+  const uint32_t* mine = p.signal[p.rank] + base;
+  const uint64_t t0 = globaltimer_ns();
+  for (int k = 0; k < p.world; ++k) {
+    for (uint32_t i = 0;; ++i) {
+      if ((int32_t)(ld_acquire_sys(mine + k) - p.epoch) >= 0) break;
+      __nanosleep(128);
+      if ((i & 63u) == 63u && globaltimer_ns() - t0 > p.wait_limit_ns) return false;
+    }
+  }
+  return true;
+}
+
+template <typename Tin, int K, int GL, bool E4M3>
+__global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_ar_kernel(const ArParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const ArLayout L = ar_layout(p.D, p.row_bytes, p.world, p.stages);
+  const int T = p.team_threads;
+  const int tt = threadIdx.x;
+  const int lane = tt & 31;
+  const int twarp = tt >> 5;
+  const int S = p.stages;
+  const int W = p.world;
+  const uint32_t slot_bytes = (uint32_t)(W + 1) * p.row_bytes;
+  const float4* sg = reinterpret_cast<const float4*>(smem + L.gamma);
+  uint8_t* ring = smem + L.slots;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
+  double* red = reinterpret_cast<double*>(smem + L.red);
+  __shared__ int s_fail;
+
+  const int64_t G = gridDim.x;
+  const int64_t slab = p.row_end - p.row_begin;
+  const int64_t nrows = blockIdx.x < slab ? (slab - 1 - blockIdx.x) / G + 1 : 0;
+  const uint64_t pol = policy_evict_first();
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
+  // Start barrier: partials complete, previous outputs consumed, on all ranks.
+  if (tt == 0) {
+    s_fail = ar_barrier(p, 0) ? 0 : 1;
+    for (int s = 0; s < S; ++s) mbar_init(smem_u32(&bars[s]), 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  __syncthreads();
+  if (s_fail) {
+    if (tt == 0 && p.status) atomicExch(p.status, (int)FARQ_ERR_DEVICE_TIMEOUT);
+    return;
+  }
+
+  auto fill = [&](int slot, int64_t row) {
+    const uint32_t bar = smem_u32(&bars[slot]);
+    const uint32_t dst = smem_u32(ring + (size_t)slot * slot_bytes);
+    mbar_arrive_expect_tx(bar, slot_bytes);
+    for (int k = 0; k < W; ++k)
+      bulk_load(dst + (uint32_t)k * p.row_bytes, p.part[k] + row * p.row_bytes, p.row_bytes, bar,
+                pol);
+    bulk_load(dst + (uint32_t)W * p.row_bytes, p.res + row * p.row_bytes, p.row_bytes, bar, pol);
+  };
+  if (tt == 0)
+    for (int s = 0; s < S && s < nrows; ++s) fill(s, p.row_begin + blockIdx.x + (int64_t)s * G);
+  for (int v = tt; v < p.nvec; v += blockDim.x) {
+    float g[8];
+    load_gamma8(p.gamma, v, p.gamma_dtype, g);
+    float4* d = reinterpret_cast<float4*>(smem + L.gamma);
+    d[v] = make_float4(g[0], g[1], g[2], g[3]);
+    d[p.nvec + v] = make_float4(g[4], g[5], g[6], g[7]);
+  }
+  __syncthreads();
+
+  const float qmax = E4M3 ? 448.0f : 127.0f;
+  const int nvec = p.nvec;
+  const int tw = T >> 5;
+  const int xdt = std::is_same<Tin, __nv_bfloat16>::value ? FARQ_DTYPE_BF16 : FARQ_DTYPE_FP16;
+  const int groups = p.D / (GL * 8);
+  bool failed = false;
+  int64_t consumed = nrows;                       // rows whose copy was waited for
+  int64_t issued = nrows < S ? nrows : (int64_t)S;  // rows whose copy was queued
+  int s = 0;
+  uint32_t parity = 0;
+
+  for (int64_t n = 0; n < nrows; ++n) {
+    const int64_t row = p.row_begin + blockIdx.x + n * G;
+    const bool ok = mbar_wait_bounded(smem_u32(&bars[s]), parity, p.wait_limit_ns);
+    if (__syncthreads_or(!ok)) {
+      if (tt == 0 && p.status) atomicExch(p.status, (int)FARQ_ERR_DEVICE_TIMEOUT);
+      failed = true;
+      consumed = n;
+      break;
+    }
+    const uint8_t* slot = ring + (size_t)s * slot_bytes;
+    const uint8_t* sr = slot + (size_t)W * p.row_bytes;
+
+    // ---- phase 1: x = sum of partials (rank order), r = x + residual
+    float w[K][8];
+    float gmax[K];
+    double ss0 = 0.0, ss1 = 0.0;
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int v = k * T + tt;
+      float m = 0.f;
+      if (v < nvec) {
+        float a[8], b[8], t[8];
+        Unpack<Tin>::run(reinterpret_cast<const uint4*>(slot)[v], a);
+        for (int rk = 1; rk < W; ++rk) {
+          Unpack<Tin>::run(reinterpret_cast<const uint4*>(slot + (size_t)rk * p.row_bytes)[v], t);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) a[e] += t[e];
+        }
+        // the all-reduced activation in the input dtype
+        const uint4 xr = make_uint4(pack2(a[0], a[1], xdt), pack2(a[2], a[3], xdt),
+                                    pack2(a[4], a[5], xdt), pack2(a[6], a[7], xdt));
+        Unpack<Tin>::run(xr, a);
+        Unpack<Tin>::run(reinterpret_cast<const uint4*>(sr)[v], b);
+        const float4 g0 = sg[v], g1 = sg[nvec + v];
+        const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          a[e] = a[e] + b[e];
+          if (e & 1)
+            ss1 = fma((double)a[e], (double)a[e], ss1);
+          else
+            ss0 = fma((double)a[e], (double)a[e], ss0);
+          w[k][e] = a[e] * g[e];
+          m = fmaxf(m, fabsf(w[k][e]));
+        }
+        for (int rk = 0; rk < W; ++rk) store8(p.rout[rk] + row * p.row_bytes, v, a, xdt);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) w[k][e] = 0.f;
+      }
+#pragma unroll
+      for (int o = 1; o < GL; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      gmax[k] = m;
+    }
+    double ss = ss0 + ss1;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) red[twarp] = ss;
+    __syncthreads();
+    if (n + S < nrows) {
+      if (tt == 0) fill(s, row + (int64_t)S * G);
+      ++issued;
+    }
+
+    double total = 0.0;
+    for (int j = 0; j < tw; ++j) total += red[j];
+    const float inv_rms =
+        __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(__double2float_rn(total), (float)p.D), p.eps)));
+    const float step = __fdiv_rn(inv_rms, qmax);
+
+    // ---- phase 2
+#pragma unroll
+    for (int k = 0; k < K; ++k) {
+      const int v = k * T + tt;
+      if (v < nvec) {
+        float sc = fmaxf(gmax[k] * step, 1.0e-12f);
+        sc = p.ue8m0 ? pow2_ceil(sc) : sc;
+        const float isc = __frcp_rn(sc);
+        float nrm[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) nrm[e] = w[k][e] * inv_rms;
+        if (p.nout[0])
+          for (int rk = 0; rk < W; ++rk)
+            store8(p.nout[rk] + row * (int64_t)p.D * (p.nout_dtype == FARQ_DTYPE_FP32 ? 4 : 2), v,
+                   nrm, p.nout_dtype);
+        uint32_t lo, hi;
+        if (E4M3) {
+          lo = e4m3x2(nrm[0] * isc, nrm[1] * isc) | (e4m3x2(nrm[2] * isc, nrm[3] * isc) << 16);
+          hi = e4m3x2(nrm[4] * isc, nrm[5] * isc) | (e4m3x2(nrm[6] * isc, nrm[7] * isc) << 16);
+        } else {
+          lo = i8(nrm[0] * isc) | (i8(nrm[1] * isc) << 8) | (i8(nrm[2] * isc) << 16) |
+               (i8(nrm[3] * isc) << 24);
+          hi = i8(nrm[4] * isc) | (i8(nrm[5] * isc) << 8) | (i8(nrm[6] * isc) << 16) |
+               (i8(nrm[7] * isc) << 24);
+        }
+        for (int rk = 0; rk < W; ++rk) {
+          st_cs_v2(p.q[rk] + row * (int64_t)p.D + 8 * (int64_t)v, lo, hi);
+          if ((lane & (GL - 1)) == 0) st_cs_f32(p.scale[rk] + row * groups + v / GL, sc);
+        }
+      }
+    }
+    if (++s == S) {
+      s = 0;
+      parity ^= 1u;
+    }
+  }
+
+  if (failed) {
+    // drain the copies still armed for this CTA's slots (bounded), then leave
+    // without the end barrier: a peer did not deliver.
+    __syncthreads();
+    if (tt == 0)
+      for (int64_t j = consumed; j < issued; ++j)
+        (void)mbar_wait_bounded(smem_u32(&bars[j % S]), (uint32_t)((j / S) & 1), p.wait_limit_ns);
+    return;
+  }
+  // End barrier: this CTA's stores to every rank are visible system-wide
+  // before it signals; the kernel completes only after every rank's CTA of
+  // the same index has signalled, i.e. after all writes into this rank landed.
+  __threadfence_system();
+  __syncthreads();
+  if (tt == 0) {
+    if (!ar_barrier(p, 1) && p.status) atomicExch(p.status, (int)FARQ_ERR_DEVICE_TIMEOUT);
+  }
+}
+
+using ArKernelFn = void (*)(const ArParams);
+ArKernelFn ar_kernel_bf16_int8(int K, int gl_log2);
+ArKernelFn ar_kernel_bf16_e4m3(int K, int gl_log2);
+ArKernelFn ar_kernel_fp16_int8(int K, int gl_log2);
+ArKernelFn ar_kernel_fp16_e4m3(int K, int gl_log2);
+
+}  // namespace farq
+
+#define FARQ_AR_KERNEL_TABLE(NAME, TIN, E4M3)                                           \
+  namespace farq {                                                                      \
+  template <int K>                                                                      \
+  static ArKernelFn NAME##_k(int gl_log2) {                                             \
+    switch (gl_log2) {                                                                  \
+      case 0: return farq_ar_kernel<TIN, K, 1, E4M3>;                                   \
+      case 1: return farq_ar_kernel<TIN, K, 2, E4M3>;                                   \
+      case 2: return farq_ar_kernel<TIN, K, 4, E4M3>;                                   \
+      case 3: return farq_ar_kernel<TIN, K, 8, E4M3>;                                   \
+      case 4: return farq_ar_kernel<TIN, K, 16, E4M3>;                                  \
+      default: return farq_ar_kernel<TIN, K, 32, E4M3>;                                 \
+    }                                                                                   \
+  }                                                                                     \
+  ArKernelFn NAME(int K, int gl_log2) {                                                 \
+    switch (K) {                                                                        \
+      case 1: return NAME##_k<1>(gl_log2);                                              \
+      case 2: return NAME##_k<2>(gl_log2);                                              \
+      case 3: return NAME##_k<3>(gl_log2);                                              \
+      case 4: return NAME##_k<4>(gl_log2);                                              \
+      case 5: return NAME##_k<5>(gl_log2);                                              \
+      case 6: return NAME##_k<6>(gl_log2);                                              \
+      case 7: return NAME##_k<7>(gl_log2);                                              \
+      default: return NAME##_k<8>(gl_log2);                                             \
+    }                                                                                   \
+  }                                                                                     \
+  }

@@ -158,6 +158,64 @@ int farq_plan(int64_t M, int64_t D, int32_t group_size, int32_t x_dtype,
               int32_t tune_ctas_per_sm, int32_t tune_teams_per_cta,
               int32_t tune_stages, int32_t tune_vec_per_thread, int64_t out[6]);
 
+/* ------------------------------------------------------------------------
+ * Tensor-parallel variant: all-reduce fused with the operator.
+ *
+ * Every rank of a W-rank group (W <= 8, one GPU each, peers reachable over
+ * NVLink) holds a partial activation P_k [M, D]; x = sum of the partials,
+ * rounded once to x_dtype, and the operator above is applied to x with the
+ * rank's residual. Rank `rank` computes the rows [rank*M/W slab] and writes
+ * every output row to all W ranks' output buffers, so on return every rank
+ * holds the full residual_out, x_q, x_scale (and norm_out) — the replicated
+ * result an all-reduce followed by the operator would give.
+ *
+ * All arrays are indexed by rank and hold pointers valid on THIS device
+ * (peer mappings, e.g. from symmetric memory). Tensors are contiguous:
+ * [M, D] activations, [M, D/G] row-major scales. `signal[k]` is rank k's
+ * zero-initialised signal buffer of FARQ_AR_SIGNAL_WORDS uint32 words, used
+ * only by this entry point; `epoch` must increase by one per call (starting
+ * at 1) and be the same on every rank. Every rank must make the same call
+ * (same M, D, dtypes, tuning); each blocks on the others inside the kernel
+ * with waits bounded at 2 s, after which the status word (if any) is set to
+ * FARQ_ERR_DEVICE_TIMEOUT.
+ *
+ * No counterpart in the reference, which runs on one device; this is the
+ * producer-side fusion of the all-reduce that precedes
+ * fused_add_rmsnorm_group_quant (task01…py:1731) in tensor-parallel models.
+ * ---------------------------------------------------------------------- */
+#define FARQ_AR_MAX_WORLD 8
+#define FARQ_AR_SIGNAL_WORDS (2 * 1024 * 8)
+
+typedef struct farq_ar_args {
+    uint32_t struct_size;          /* = sizeof(farq_ar_args_t)                */
+    int32_t  x_dtype;              /* BF16 | FP16: partials, residual, residual_out */
+    int32_t  gamma_dtype;          /* BF16 | FP16 | FP32                       */
+    int32_t  norm_out_dtype;       /* BF16 | FP16 | FP32 (ignored if no norm_out) */
+    int32_t  q_dtype;              /* INT8 | E4M3                              */
+    int32_t  flags;                /* FARQ_FLAG_UE8M0                          */
+    int32_t  group_size;
+    int32_t  world;                /* W, 1..8                                  */
+    int32_t  rank;                 /* this rank, 0..W-1                        */
+    uint32_t epoch;                /* 1, 2, 3, ... identical on every rank     */
+    int64_t  M;
+    int64_t  D;
+    float    eps;
+    int32_t  reserved0;            /* must be 0                                */
+    const void* partial[FARQ_AR_MAX_WORLD];      /* [M, D] per rank           */
+    const void* residual;                        /* [M, D] on this rank       */
+    const void* gamma;                           /* [D] on this rank          */
+    void*    residual_out[FARQ_AR_MAX_WORLD];    /* [M, D] per rank           */
+    void*    norm_out[FARQ_AR_MAX_WORLD];        /* [M, D] per rank, or all NULL */
+    void*    x_q[FARQ_AR_MAX_WORLD];             /* [M, D] per rank           */
+    float*   x_scale[FARQ_AR_MAX_WORLD];         /* [M, D/G] per rank         */
+    uint32_t* signal[FARQ_AR_MAX_WORLD];         /* per rank                  */
+    int32_t* status;                             /* device int or NULL        */
+} farq_ar_args_t;
+
+/* Launch the fused all-reduce + operator on `stream` of the current device.
+ * Returns a farq_status; validation errors are reported before any launch. */
+int farq_ar_launch(const farq_ar_args_t* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

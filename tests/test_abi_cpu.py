@@ -29,7 +29,7 @@ def declared_functions():
 def test_header_declares_entry_points():
     names = declared_functions()
     assert {"farq_launch", "farq_strerror", "farq_abi_version", "farq_max_hidden",
-            "farq_plan"} <= set(names)
+            "farq_plan", "farq_ar_launch"} <= set(names)
 
 
 def test_library_exports_every_declared_symbol(lib):
@@ -110,3 +110,21 @@ def test_python_wrapper_refuses_cpu_tensors():
         fused_add_rmsnorm_group_quant(x, x, torch.ones(256, dtype=torch.bfloat16), x.clone(), None,
                                       torch.zeros(2, 256, dtype=torch.int8),
                                       torch.zeros(2, 2), 1e-6, 128)
+
+
+def test_ar_entry_validation_codes(lib):
+    from flagos_kernelgen_72h_shanghai_2026_b200.tp import FarqArArgs
+    a = FarqArArgs()
+    a.struct_size = ctypes.sizeof(a) + 4
+    assert lib.farq_ar_launch(ctypes.byref(a), None) == _lib.ERR_BAD_ARGS_SIZE
+    a = FarqArArgs()
+    a.struct_size = ctypes.sizeof(a)
+    a.x_dtype, a.gamma_dtype, a.q_dtype, a.group_size = _lib.DTYPE_BF16, _lib.DTYPE_BF16, _lib.DTYPE_E4M3, 128
+    a.M, a.D, a.world, a.rank = 8, 1024, 2, 2
+    assert lib.farq_ar_launch(ctypes.byref(a), None) == _lib.ERR_BAD_SHAPE  # rank >= world
+    a.rank, a.world = 0, 9
+    assert lib.farq_ar_launch(ctypes.byref(a), None) == _lib.ERR_BAD_SHAPE  # world > 8
+    a.world = 2
+    assert lib.farq_ar_launch(ctypes.byref(a), None) == _lib.ERR_NULL_POINTER
+    a.M = 0
+    assert lib.farq_ar_launch(ctypes.byref(a), None) == _lib.OK
