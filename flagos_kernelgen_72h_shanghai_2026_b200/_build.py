@@ -16,7 +16,7 @@ REPO_DIR = PKG_DIR.parent
 INCLUDE_DIR = REPO_DIR / "include"
 CSRC_DIR = PKG_DIR / "csrc"
 SOURCES = [CSRC_DIR / "farq.cu", *sorted(CSRC_DIR.glob("farq_inst_*.cu")),
-           *sorted(CSRC_DIR.glob("farq_ar_inst_*.cu"))]
+           *sorted(CSRC_DIR.glob("farq_ar_inst_*.cu")), CSRC_DIR / "farq_noalloc.cu"]
 HEADERS = [INCLUDE_DIR / "farq.h", CSRC_DIR / "farq_kernel.cuh", CSRC_DIR / "farq_ar_kernel.cuh"]
 LIB_PATH = PKG_DIR / "libfarq.so"
 

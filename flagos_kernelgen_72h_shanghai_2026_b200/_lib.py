@@ -29,6 +29,7 @@ ERR_UNSUPPORTED = 6
 ERR_CUDA = 7
 ERR_BAD_ARGS_SIZE = 8
 ERR_DEVICE_TIMEOUT = 9
+ERR_NOALLOC_TOO_LARGE = 10
 
 ABI_VERSION = 1
 

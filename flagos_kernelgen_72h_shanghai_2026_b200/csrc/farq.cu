@@ -219,6 +219,8 @@ const char* farq_strerror(int status) {
     case FARQ_ERR_CUDA: return "a CUDA runtime call failed";
     case FARQ_ERR_BAD_ARGS_SIZE: return "farq_args_t size mismatch (header and library differ)";
     case FARQ_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait ran out";
+    case FARQ_ERR_NOALLOC_TOO_LARGE:
+      return "call needs more than the 64 MiB staging array of farq_launch_host_noalloc; split the rows";
     default: return "unknown farq status";
   }
 }

@@ -75,7 +75,9 @@ enum farq_status {
     FARQ_ERR_UNSUPPORTED = 6,      /* D or a tuning choice out of range      */
     FARQ_ERR_CUDA = 7,             /* a CUDA runtime call failed             */
     FARQ_ERR_BAD_ARGS_SIZE = 8,    /* struct_size does not match this build  */
-    FARQ_ERR_DEVICE_TIMEOUT = 9    /* a bounded device wait ran out          */
+    FARQ_ERR_DEVICE_TIMEOUT = 9,   /* a bounded device wait ran out          */
+    FARQ_ERR_NOALLOC_TOO_LARGE = 10 /* call needs more than the 64 MiB staging
+                                       array of farq_launch_host_noalloc     */
 };
 
 /*
@@ -157,6 +159,29 @@ int64_t farq_max_hidden(void);
 int farq_plan(int64_t M, int64_t D, int32_t group_size, int32_t x_dtype,
               int32_t tune_ctas_per_sm, int32_t tune_teams_per_cta,
               int32_t tune_stages, int32_t tune_vec_per_thread, int64_t out[6]);
+
+/*
+ * farq_launch with HOST buffers and no device allocation: x, residual, gamma,
+ * residual_out, norm_out (or NULL), x_q and x_scale in `args` are host
+ * pointers (pinned memory keeps the copies asynchronous); the call copies the
+ * inputs into a device array compiled into the library, runs the kernel and
+ * copies the outputs back, all queued on `stream`. The outputs are valid once
+ * the stream has been synchronised.
+ *
+ * For callers that cannot allocate GPU memory: plugins inside a process whose
+ * device allocator belongs to another framework, or C/FFI callers that only
+ * hold host buffers. The array holds 64 MiB on every GPU that loads the
+ * library, until the process exits; a call needing more staging (inputs,
+ * gamma and outputs of all M rows, each rounded up to 256 bytes — about
+ * 1,330 rows at D = 7168, bf16 -> e4m3) returns FARQ_ERR_NOALLOC_TOO_LARGE;
+ * split the rows. Tensors must be contiguous with row-major x_scale. The
+ * first call on a device looks up the array's device address (make it before
+ * any stream capture). All calls share the array: calls that overlap on the
+ * GPU race; calls on one stream are ordered.
+ *
+ * No counterpart in the reference, which has no host-buffer path.
+ */
+int farq_launch_host_noalloc(const farq_args_t* args, void* stream);
 
 /* ------------------------------------------------------------------------
  * Tensor-parallel variant: all-reduce fused with the operator.
