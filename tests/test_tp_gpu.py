@@ -86,7 +86,8 @@ def test_tp_fused_world1(cuda_dev):
     _run(1, 333, 7168)
 
 
-def test_tp_fused_world2():
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
-    _run(2, 1001, 7168)
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_fused_multi_gpu(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    _run(world, 1001, 7168)
