@@ -322,6 +322,17 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_rows_kernel(const Para
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
+  // gamma -> fp32 shared memory, once per CTA, in two planes (elements 0-3,
+  // then 4-7 of every vector) so that a warp's 16-byte reads of one plane are
+  // contiguous (no bank conflicts). The first round of gamma loads is issued
+  // before the row copies: queued behind the copies of all CTAs it would
+  // arrive microseconds after the rows and hold back the first row.
+  float4* gs = reinterpret_cast<float4*>(smem + L.gamma);
+  float g_first[8];
+  const bool has_first = threadIdx.x < p.nvec;
+  if (has_first) load_gamma8(p.gamma, threadIdx.x, p.gamma_dtype, g_first);
+  __syncthreads();  // every thread's first gamma load is issued (not yet complete)
+
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) mbar_init(smem_u32(&bars[s]), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -338,15 +349,15 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_rows_kernel(const Para
       }
     }
   }
-  // gamma -> fp32 shared memory, once per CTA (overlaps the first copies),
-  // in two planes (elements 0-3, then 4-7 of every vector) so that a warp's
-  // 16-byte reads of one plane are contiguous (no bank conflicts).
-  for (int v = threadIdx.x; v < p.nvec; v += blockDim.x) {
+  if (has_first) {
+    gs[threadIdx.x] = make_float4(g_first[0], g_first[1], g_first[2], g_first[3]);
+    gs[p.nvec + threadIdx.x] = make_float4(g_first[4], g_first[5], g_first[6], g_first[7]);
+  }
+  for (int v = threadIdx.x + blockDim.x; v < p.nvec; v += blockDim.x) {
     float g[8];
     load_gamma8(p.gamma, v, p.gamma_dtype, g);
-    float4* d = reinterpret_cast<float4*>(smem + L.gamma);
-    d[v] = make_float4(g[0], g[1], g[2], g[3]);
-    d[p.nvec + v] = make_float4(g[4], g[5], g[6], g[7]);
+    gs[v] = make_float4(g[0], g[1], g[2], g[3]);
+    gs[p.nvec + v] = make_float4(g[4], g[5], g[6], g[7]);
   }
   __syncthreads();
 
