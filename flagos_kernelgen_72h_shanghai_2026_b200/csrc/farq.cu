@@ -23,6 +23,7 @@ std::atomic<int> g_sm_count[kMaxDevices];
 std::atomic<int> g_smem_optin[kMaxDevices];
 std::atomic<int> g_smem_set[kMaxDevices][kSlots];  // largest dynamic smem granted
 std::atomic<int> g_regs[kMaxDevices][kSlots];      // registers per thread (0 = unknown)
+std::atomic<int> g_ar_smem_set[kMaxDevices][kSlots];  // same, tensor-parallel kernels
 
 int ilog2(int v) {
   int l = 0;
@@ -403,9 +404,13 @@ int farq_ar_launch(const farq_ar_args_t* a, void* stream) {
   else
     fn = e4m3 ? ar_kernel_fp16_e4m3(K, gl) : ar_kernel_fp16_int8(K, gl);
   const size_t smem = ar_layout((int)D, row_bytes, W, S).total;
-  if (cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-    return FARQ_ERR_CUDA;
+  const int slot = (((a->x_dtype == FARQ_DTYPE_BF16 ? 0 : 1) * 2 + (e4m3 ? 1 : 0)) * kMaxK + (K - 1)) * 6 + gl;
+  if ((int)smem > g_ar_smem_set[dev][slot].load(std::memory_order_relaxed)) {
+    if (cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+      return FARQ_ERR_CUDA;
+    g_ar_smem_set[dev][slot].store((int)smem, std::memory_order_relaxed);
+  }
 
   ArParams p = {};
   for (int k = 0; k < W; ++k) {

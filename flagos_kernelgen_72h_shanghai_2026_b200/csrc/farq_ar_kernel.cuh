@@ -73,30 +73,37 @@ __host__ __device__ inline ArLayout ar_layout(int D, uint32_t row_bytes, int wor
   return L;
 }
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
   uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ void fence_acq_rel_sys() {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
 
-// Cross-rank barrier of CTA blockIdx.x for `phase`: signal every rank, then
-// wait (bounded) until every rank has signalled this CTA. Returns false when
-// the wait ran out. Called by one thread.
+// Cross-rank barrier of CTA blockIdx.x for `phase`, run by one thread: signal
+// every rank, then wait (bounded) until every rank has signalled this CTA.
+// The caller orders what must precede the signal (every thread's
+// fence_acq_rel_sys and a CTA barrier, before the end barrier); the fence after the wait
+// orders the peers' earlier writes before this CTA's later accesses.
+// Returns false when the wait ran out.
 __device__ __forceinline__ bool ar_barrier(const ArParams& p, int phase) {
   const size_t base = ((size_t)phase * kMaxArCtas + blockIdx.x) * kMaxWorld;
-  for (int k = 0; k < p.world; ++k) st_release_sys(p.signal[k] + base + p.rank, p.epoch);
+  for (int k = 0; k < p.world; ++k) st_relaxed_sys(p.signal[k] + base + p.rank, p.epoch);
   const uint32_t* mine = p.signal[p.rank] + base;
   const uint64_t t0 = globaltimer_ns();
   for (int k = 0; k < p.world; ++k) {
     for (uint32_t i = 0;; ++i) {
-      if ((int32_t)(ld_acquire_sys(mine + k) - p.epoch) >= 0) break;
-      __nanosleep(128);
-      if ((i & 63u) == 63u && globaltimer_ns() - t0 > p.wait_limit_ns) return false;
+      if ((int32_t)(ld_relaxed_sys(mine + k) - p.epoch) >= 0) break;
+      __nanosleep(20);
+      if ((i & 255u) == 255u && globaltimer_ns() - t0 > p.wait_limit_ns) return false;
     }
   }
+  fence_acq_rel_sys();
   return true;
 }
 
@@ -123,30 +130,32 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_ar_kernel(const ArPara
   const uint64_t pol = policy_evict_first();
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
-  // Start barrier: partials complete, previous outputs consumed, on all ranks.
+  // Residual rows and gamma are this rank's own data: their loads are issued
+  // before the start barrier. Partials are read only after it.
   if (tt == 0) {
-    s_fail = ar_barrier(p, 0) ? 0 : 1;
     for (int s = 0; s < S; ++s) mbar_init(smem_u32(&bars[s]), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
-  __syncthreads();
-  if (s_fail) {
-    if (tt == 0 && p.status) atomicExch(p.status, (int)FARQ_ERR_DEVICE_TIMEOUT);
-    return;
-  }
-
-  auto fill = [&](int slot, int64_t row) {
+  auto fill_res = [&](int slot, int64_t row) {
     const uint32_t bar = smem_u32(&bars[slot]);
     const uint32_t dst = smem_u32(ring + (size_t)slot * slot_bytes);
-    mbar_arrive_expect_tx(bar, slot_bytes);
+    mbar_arrive_expect_tx(bar, slot_bytes);  // the whole slot: residual + W partials
+    bulk_load(dst + (uint32_t)W * p.row_bytes, p.res + row * p.row_bytes, p.row_bytes, bar, pol);
+  };
+  auto fill_parts = [&](int slot, int64_t row) {
+    const uint32_t bar = smem_u32(&bars[slot]);
+    const uint32_t dst = smem_u32(ring + (size_t)slot * slot_bytes);
     for (int k = 0; k < W; ++k)
       bulk_load(dst + (uint32_t)k * p.row_bytes, p.part[k] + row * p.row_bytes, p.row_bytes, bar,
                 pol);
-    bulk_load(dst + (uint32_t)W * p.row_bytes, p.res + row * p.row_bytes, p.row_bytes, bar, pol);
+  };
+  auto fill = [&](int slot, int64_t row) {
+    fill_res(slot, row);
+    fill_parts(slot, row);
   };
   if (tt == 0)
-    for (int s = 0; s < S && s < nrows; ++s) fill(s, p.row_begin + blockIdx.x + (int64_t)s * G);
+    for (int s = 0; s < S && s < nrows; ++s) fill_res(s, p.row_begin + blockIdx.x + (int64_t)s * G);
   for (int v = tt; v < p.nvec; v += blockDim.x) {
     float g[8];
     load_gamma8(p.gamma, v, p.gamma_dtype, g);
@@ -154,7 +163,30 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_ar_kernel(const ArPara
     d[v] = make_float4(g[0], g[1], g[2], g[3]);
     d[p.nvec + v] = make_float4(g[4], g[5], g[6], g[7]);
   }
+  // Start barrier: every rank's partial is complete and every rank has
+  // finished with the previous contents of its output buffers.
+  if (tt == 0) {
+    s_fail = ar_barrier(p, 0) ? 0 : 1;
+    if (!s_fail)
+      for (int s = 0; s < S && s < nrows; ++s)
+        fill_parts(s, p.row_begin + blockIdx.x + (int64_t)s * G);
+  }
   __syncthreads();
+  if (s_fail) {
+    // drain the residual copies already queued (bounded), then leave
+    if (tt == 0) {
+      if (p.status) atomicExch(p.status, (int)FARQ_ERR_DEVICE_TIMEOUT);
+      for (int s = 0; s < S && s < nrows; ++s) {
+        // the slot's phase expects W more rows that will never be sent:
+        // complete the transaction count with the missing bytes instead
+        asm volatile("mbarrier.complete_tx.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&bars[s])),
+                     "r"((uint32_t)W * p.row_bytes)
+                     : "memory");
+        (void)mbar_wait_bounded(smem_u32(&bars[s]), 0, p.wait_limit_ns);
+      }
+    }
+    return;
+  }
 
   const float qmax = E4M3 ? 448.0f : 127.0f;
   const int nvec = p.nvec;
@@ -286,7 +318,7 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_ar_kernel(const ArPara
   // End barrier: this CTA's stores to every rank are visible system-wide
   // before it signals; the kernel completes only after every rank's CTA of
   // the same index has signalled, i.e. after all writes into this rank landed.
-  __threadfence_system();
+  fence_acq_rel_sys();  // each thread: its stores to every rank before the signal
   __syncthreads();
   if (tt == 0) {
     if (!ar_barrier(p, 1) && p.status) atomicExch(p.status, (int)FARQ_ERR_DEVICE_TIMEOUT);

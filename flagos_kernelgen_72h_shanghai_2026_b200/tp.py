@@ -115,6 +115,29 @@ class TPFusedNormQuant:
         self._handle = symm.rendezvous(self._arena, self.group.group_name)
         self._peers = [int(p) for p in self._handle.buffer_ptrs]
         self.epoch = 0
+        # Per-call work is kept small: the argument struct with every peer
+        # pointer is built once, only M, epoch, residual, gamma change.
+        a = FarqArArgs()
+        a.struct_size = ctypes.sizeof(FarqArArgs)
+        a.x_dtype = _DT[self.dtype]
+        a.norm_out_dtype = _DT[self.norm_dtype] if self.norm_dtype else 0
+        a.q_dtype = _Q[self.q_dtype]
+        a.group_size = self.G
+        a.world = self.world
+        a.rank = self.rank
+        a.D = self.D
+        L = self._layout
+        for k, base in enumerate(self._peers):
+            a.partial[k] = base + L["partial"]
+            a.residual_out[k] = base + L["residual_out"]
+            a.norm_out[k] = base + L["norm_out"] if self.norm_dtype else None
+            a.x_q[k] = base + L["x_q"]
+            a.x_scale[k] = base + L["x_scale"]
+            a.signal[k] = base + L["signal"]
+        self._args = a
+        self._args_ref = ctypes.byref(a)
+        self._views = {}
+        self._lib = _lib.load()
         dist.barrier(group=self.group)
 
     def _view(self, name, dtype, shape):
@@ -151,33 +174,20 @@ class TPFusedNormQuant:
         if gamma.shape != (self.D,) or gamma.dtype not in _DT:
             raise ValueError("gamma must be a [D] float tensor")
         self.epoch += 1
-        a = FarqArArgs()
-        a.struct_size = ctypes.sizeof(FarqArArgs)
-        a.x_dtype = _DT[self.dtype]
+        a = self._args
         a.gamma_dtype = _DT[gamma.dtype]
-        a.norm_out_dtype = _DT[self.norm_dtype] if self.norm_dtype else 0
-        a.q_dtype = _Q[self.q_dtype]
         a.flags = _lib.FLAG_UE8M0 if ue8m0 else 0
-        a.group_size = self.G
-        a.world = self.world
-        a.rank = self.rank
         a.epoch = self.epoch & 0xFFFFFFFF
         a.M = M
-        a.D = self.D
         a.eps = float(eps)
-        L = self._layout
-        for k, base in enumerate(self._peers):
-            a.partial[k] = base + L["partial"]
-            a.residual_out[k] = base + L["residual_out"]
-            a.norm_out[k] = base + L["norm_out"] if self.norm_dtype else None
-            a.x_q[k] = base + L["x_q"]
-            a.x_scale[k] = base + L["x_scale"]
-            a.signal[k] = base + L["signal"]
         a.residual = residual.data_ptr()
         a.gamma = gamma.data_ptr()
         a.status = status.data_ptr() if status is not None else None
-        lib = _lib.load()
-        st = lib.farq_ar_launch(ctypes.byref(a), torch.cuda.current_stream(self.device).cuda_stream)
+        st = self._lib.farq_ar_launch(self._args_ref,
+                                      torch.cuda.current_stream(self.device).cuda_stream)
         if st != _lib.OK:
             raise RuntimeError(f"farq_ar_launch failed: {_lib.strerror(st)} (status {st})")
-        return self.outputs(M)
+        out = self._views.get(M)
+        if out is None:
+            out = self._views[M] = self.outputs(M)
+        return out
