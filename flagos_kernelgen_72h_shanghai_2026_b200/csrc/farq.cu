@@ -439,8 +439,9 @@ int farq_ar_launch(const farq_ar_args_t* a, void* stream) {
   p.nout_dtype = a->norm_out_dtype;
   p.ue8m0 = (a->flags & FARQ_FLAG_UE8M0) ? 1 : 0;
   p.epoch = a->epoch;
+  p.force_timeout = (a->flags & FARQ_FLAG_TEST_FORCE_TIMEOUT) ? 1 : 0;
   p.eps = a->eps;
-  p.wait_limit_ns = kWaitLimitNs;
+  p.wait_limit_ns = p.force_timeout ? kTestWaitLimitNs : kWaitLimitNs;
   void* kargs[] = {&p};
   if (cudaLaunchKernel(reinterpret_cast<const void*>(fn), dim3((unsigned)grid), dim3(T), kargs,
                        smem, static_cast<cudaStream_t>(stream)) != cudaSuccess)

@@ -54,6 +54,7 @@ struct ArParams {
   uint32_t row_bytes;              // D * sizeof(x element)
   int32_t gamma_dtype, nout_dtype, ue8m0;
   uint32_t epoch;
+  int32_t force_timeout;
   float eps;
   uint64_t wait_limit_ns;
 };
@@ -91,14 +92,14 @@ __device__ __forceinline__ void fence_acq_rel_sys() {
 // fence_acq_rel_sys and a CTA barrier, before the end barrier); the fence after the wait
 // orders the peers' earlier writes before this CTA's later accesses.
 // Returns false when the wait ran out.
-__device__ __forceinline__ bool ar_barrier(const ArParams& p, int phase) {
+__device__ __forceinline__ bool ar_barrier(const ArParams& p, int phase, uint32_t want) {
   const size_t base = ((size_t)phase * kMaxArCtas + blockIdx.x) * kMaxWorld;
   for (int k = 0; k < p.world; ++k) st_relaxed_sys(p.signal[k] + base + p.rank, p.epoch);
   const uint32_t* mine = p.signal[p.rank] + base;
   const uint64_t t0 = globaltimer_ns();
   for (int k = 0; k < p.world; ++k) {
     for (uint32_t i = 0;; ++i) {
-      if ((int32_t)(ld_relaxed_sys(mine + k) - p.epoch) >= 0) break;
+      if ((int32_t)(ld_relaxed_sys(mine + k) - want) >= 0) break;
       __nanosleep(20);
       if ((i & 255u) == 255u && globaltimer_ns() - t0 > p.wait_limit_ns) return false;
     }
@@ -166,7 +167,8 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_ar_kernel(const ArPara
   // Start barrier: every rank's partial is complete and every rank has
   // finished with the previous contents of its output buffers.
   if (tt == 0) {
-    s_fail = ar_barrier(p, 0) ? 0 : 1;
+    // (test-only flag: wait for an epoch no rank will signal)
+    s_fail = ar_barrier(p, 0, p.force_timeout ? p.epoch + 0x40000000u : p.epoch) ? 0 : 1;
     if (!s_fail)
       for (int s = 0; s < S && s < nrows; ++s)
         fill_parts(s, p.row_begin + blockIdx.x + (int64_t)s * G);
@@ -321,7 +323,7 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_ar_kernel(const ArPara
   fence_acq_rel_sys();  // each thread: its stores to every rank before the signal
   __syncthreads();
   if (tt == 0) {
-    if (!ar_barrier(p, 1) && p.status) atomicExch(p.status, (int)FARQ_ERR_DEVICE_TIMEOUT);
+    if (!ar_barrier(p, 1, p.epoch) && p.status) atomicExch(p.status, (int)FARQ_ERR_DEVICE_TIMEOUT);
   }
 }
 

@@ -162,7 +162,8 @@ class TPFusedNormQuant:
         return ro, no, q, s
 
     def __call__(self, M: int, residual: torch.Tensor, gamma: torch.Tensor, eps: float, *,
-                 ue8m0: bool = False, status: torch.Tensor | None = None):
+                 ue8m0: bool = False, status: torch.Tensor | None = None,
+                 _test_force_timeout: bool = False):
         """x = sum over ranks of partial_buffer(M); returns the replicated
         (residual_out, norm_out, x_q, x_scale) of the operator on x."""
         if not 0 <= M <= self.M:
@@ -176,7 +177,8 @@ class TPFusedNormQuant:
         self.epoch += 1
         a = self._args
         a.gamma_dtype = _DT[gamma.dtype]
-        a.flags = _lib.FLAG_UE8M0 if ue8m0 else 0
+        a.flags = (_lib.FLAG_UE8M0 if ue8m0 else 0) | (
+            _lib.FLAG_TEST_FORCE_TIMEOUT if _test_force_timeout else 0)
         a.epoch = self.epoch & 0xFFFFFFFF
         a.M = M
         a.eps = float(eps)

@@ -217,7 +217,9 @@ typedef struct farq_ar_args {
     int32_t  gamma_dtype;          /* BF16 | FP16 | FP32                       */
     int32_t  norm_out_dtype;       /* BF16 | FP16 | FP32 (ignored if no norm_out) */
     int32_t  q_dtype;              /* INT8 | E4M3                              */
-    int32_t  flags;                /* FARQ_FLAG_UE8M0                          */
+    int32_t  flags;                /* FARQ_FLAG_UE8M0; FARQ_FLAG_TEST_FORCE_TIMEOUT
+                                      makes the start barrier wait (1 ms) for
+                                      an epoch no rank signals (tests only)    */
     int32_t  group_size;
     int32_t  world;                /* W, 1..8                                  */
     int32_t  rank;                 /* this rank, 0..W-1                        */

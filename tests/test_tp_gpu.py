@@ -54,6 +54,18 @@ def _worker(rank, world, port, M, D, q):
             got = dict(residual_out=ro.cpu(), norm_out=no.cpu(), x_q=xq.cpu(), x_scale=xs.cpu())
             check_outputs(got, dict(residual_out=rro, norm_out=rno, x_q=rq, x_scale=rs), "e4m3")
         assert int(status.item()) == 0
+        if world == 1:
+            # a cross-rank wait that nothing satisfies (test-only flag, 1 ms
+            # limit) reports through the status word; the next call is exact
+            op(M, residual.to(dev), gamma.to(dev), 1e-6, status=status, _test_force_timeout=True)
+            torch.cuda.synchronize(dev)
+            assert int(status.item()) == 9  # FARQ_ERR_DEVICE_TIMEOUT
+            status.zero_()
+            ro, no, xq, xs = op(M, residual.to(dev), gamma.to(dev), 1e-6, status=status)
+            torch.cuda.synchronize(dev)
+            assert int(status.item()) == 0
+            got = dict(residual_out=ro.cpu(), norm_out=no.cpu(), x_q=xq.cpu(), x_scale=xs.cpu())
+            check_outputs(got, dict(residual_out=rro, norm_out=rno, x_q=rq, x_scale=rs), "e4m3")
         dist.barrier()
         dist.destroy_process_group()
         q.put((rank, "ok"))
