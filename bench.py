@@ -352,6 +352,62 @@ def run_e2e(args, w, rows, dev, g, start, rank, pg):
     return {"ms": t0.elapsed_time(t1) / n, "h2d": h2d, "d2h": d2h}
 
 
+def run_tp(args, w, rank, world, local):
+    """Tensor-parallel variant: x = all-reduce of per-rank partials fused with
+    the operator (tp.TPFusedNormQuant), against NCCL all-reduce followed by the
+    single-GPU kernel, on the same M x D per call. Prints its own JSON line
+    (device time, max over ranks); not the default benchmark."""
+    import torch.distributed as dist
+    from flagos_kernelgen_72h_shanghai_2026_b200 import fused_add_rmsnorm_group_quant
+    from flagos_kernelgen_72h_shanghai_2026_b200._build import build_lib
+    from flagos_kernelgen_72h_shanghai_2026_b200.tp import TPFusedNormQuant
+
+    build_lib()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", "29561")
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    M, D, G = w.M, w.D, w.group_size
+    op = TPFusedNormQuant(M, D, G, dtype=w.dtype, q_dtype=w.q_dtype)
+    x, r, g = make_inputs(w, device=dev, seed_offset=rank)
+    op.partial_buffer(M).copy_(x)
+    xr = torch.empty_like(x)
+    ro, no, q, s = alloc_outputs(w, M, dev)
+
+    def fused():
+        op(M, r, g, w.eps, ue8m0=w.ue8m0)
+
+    def unfused():
+        xr.copy_(x)
+        dist.all_reduce(xr)
+        fused_add_rmsnorm_group_quant(xr, r, g, ro, no, q, s, w.eps, G, ue8m0=w.ue8m0)
+
+    res = {}
+    for name, f in (("fused", fused), ("nccl_allreduce_then_kernel", unfused)):
+        for _ in range(args.warmup):
+            f()
+        torch.cuda.synchronize(dev)
+        dist.barrier()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.steps):
+            f()
+        t1.record()
+        torch.cuda.synchronize(dev)
+        t = torch.tensor([t0.elapsed_time(t1) / args.steps * 1e3], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        res[name] = round(float(t.item()), 2)
+    if rank == 0:
+        print(json.dumps({"metric": "tensor-parallel all-reduce + add + RMSNorm + group quant, us/call",
+                          "mode": "tp", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                          "config": {"workload": w.name, "M": M, "D": D, "group_size": G},
+                          "us_per_call": res, "higher_is_better": False}), flush=True)
+    dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -359,6 +415,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=200)
     ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--mode", default="rows", choices=["rows", "tp"],
+                    help="rows: the operator on row shards (default benchmark); tp: the "
+                         "tensor-parallel variant (all-reduce fused with the operator)")
     ap.add_argument("--scaling", default=None, choices=["weak", "strong"],
                     help="weak: every GPU runs the full config (default except config 5); "
                          "strong: the config's rows are split over the GPUs (default for config 5)")
@@ -377,6 +436,9 @@ def main():
         if world == 1 and args.gpus > 1:
             ap.error("run N > 1 under torchrun (one process per GPU)")
     w = CONFIGS[args.config]
+    if args.mode == "tp":
+        run_tp(args, w, rank, world, local)
+        return
     if args.impl == "reference":
         run_reference_arm(args, w, rank, world)
     else:

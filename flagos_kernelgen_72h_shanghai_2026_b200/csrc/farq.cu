@@ -24,6 +24,7 @@ std::atomic<int> g_smem_optin[kMaxDevices];
 std::atomic<int> g_smem_set[kMaxDevices][kSlots];  // largest dynamic smem granted
 std::atomic<int> g_regs[kMaxDevices][kSlots];      // registers per thread (0 = unknown)
 std::atomic<int> g_ar_smem_set[kMaxDevices][kSlots];  // same, tensor-parallel kernels
+std::atomic<int> g_ar_regs[kMaxDevices][kSlots];
 
 int ilog2(int v) {
   int l = 0;
@@ -384,18 +385,6 @@ int farq_ar_launch(const farq_ar_args_t* a, void* stream) {
   int K, T;
   st = pick_k(D / 8, 0, false, &K, &T);
   if (st != FARQ_OK) return st;
-  // Slots of (W + 1) rows next to gamma, as many as fit (at most kMaxStages).
-  int S = kMaxStages;
-  const int64_t cap = (int64_t)optin < kSmemPerSm - kSmemReservedPerCta ? optin
-                                                                         : kSmemPerSm - kSmemReservedPerCta;
-  while (S > 0 && (int64_t)ar_layout((int)D, row_bytes, W, S).total > cap) --S;
-  if (S < 1) return FARQ_ERR_UNSUPPORTED;
-  // The grid must be the same on every rank (CTA b meets CTA b): derive it
-  // from the largest slab, ceil(M / W), not from this rank's slab.
-  int64_t grid = (M + W - 1) / W;
-  if (grid > sms) grid = sms;
-  if (grid > kMaxArCtas) grid = kMaxArCtas;
-  if (grid < 1) grid = 1;
   const int gl = ilog2(G / 8);
   ArKernelFn fn;
   const bool e4m3 = a->q_dtype == FARQ_DTYPE_E4M3;
@@ -403,8 +392,39 @@ int farq_ar_launch(const farq_ar_args_t* a, void* stream) {
     fn = e4m3 ? ar_kernel_bf16_e4m3(K, gl) : ar_kernel_bf16_int8(K, gl);
   else
     fn = e4m3 ? ar_kernel_fp16_e4m3(K, gl) : ar_kernel_fp16_int8(K, gl);
-  const size_t smem = ar_layout((int)D, row_bytes, W, S).total;
   const int slot = (((a->x_dtype == FARQ_DTYPE_BF16 ? 0 : 1) * 2 + (e4m3 ? 1 : 0)) * kMaxK + (K - 1)) * 6 + gl;
+  int regs = g_ar_regs[dev][slot].load(std::memory_order_relaxed);
+  if (regs <= 0) {
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, reinterpret_cast<const void*>(fn)) != cudaSuccess)
+      return FARQ_ERR_CUDA;
+    regs = fa.numRegs;
+    g_ar_regs[dev][slot].store(regs, std::memory_order_relaxed);
+  }
+  // Row teams as the register file allows (as in the single-GPU kernel); a
+  // CTA-wide ring of S >= teams slots of (W + 1) rows, one slot per team.
+  const int64_t cap = (int64_t)optin < kSmemPerSm - kSmemReservedPerCta ? optin
+                                                                         : kSmemPerSm - kSmemReservedPerCta;
+  int teams = kMaxCtaThreads / T;
+  const int by_regs = kRegsPerSm / (T * ((regs + 7) / 8 * 8));
+  if (by_regs < teams) teams = by_regs;
+  if (teams > kMaxTeams) teams = kMaxTeams;
+  // The launch shape must be the same on every rank (CTA b meets CTA b), so
+  // it is derived from the largest slab, ceil(M / W), not from this rank's.
+  const int64_t max_slab = (M + W - 1) / W;
+  const int64_t per_sm = (max_slab + sms - 1) / sms;
+  if (per_sm < teams) teams = (int)(per_sm < 1 ? 1 : per_sm);
+  auto fits = [&](int t, int s) {
+    return (int64_t)ar_layout((int)D, row_bytes, W, t, s).total <= cap;
+  };
+  while (teams > 1 && !fits(teams, teams)) --teams;
+  const int S = teams;
+  if (teams < 1 || !fits(teams, S)) return FARQ_ERR_UNSUPPORTED;
+  int64_t grid = (max_slab + teams - 1) / teams;
+  if (grid > sms) grid = sms;
+  if (grid > kMaxArCtas) grid = kMaxArCtas;
+  if (grid < 1) grid = 1;
+  const size_t smem = ar_layout((int)D, row_bytes, W, teams, S).total;
   if ((int)smem > g_ar_smem_set[dev][slot].load(std::memory_order_relaxed)) {
     if (cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
@@ -431,6 +451,7 @@ int farq_ar_launch(const farq_ar_args_t* a, void* stream) {
   p.D = (int32_t)D;
   p.nvec = (int32_t)(D / 8);
   p.team_threads = T;
+  p.teams = teams;
   p.stages = S;
   p.world = W;
   p.rank = a->rank;
@@ -443,7 +464,7 @@ int farq_ar_launch(const farq_ar_args_t* a, void* stream) {
   p.eps = a->eps;
   p.wait_limit_ns = p.force_timeout ? kTestWaitLimitNs : kWaitLimitNs;
   void* kargs[] = {&p};
-  if (cudaLaunchKernel(reinterpret_cast<const void*>(fn), dim3((unsigned)grid), dim3(T), kargs,
+  if (cudaLaunchKernel(reinterpret_cast<const void*>(fn), dim3((unsigned)grid), dim3(T * teams), kargs,
                        smem, static_cast<cudaStream_t>(stream)) != cudaSuccess)
     return FARQ_ERR_CUDA;
   return FARQ_OK;

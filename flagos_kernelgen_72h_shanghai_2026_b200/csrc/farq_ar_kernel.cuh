@@ -11,14 +11,16 @@
 //   then the reference per-row math on x and residual, with every output row
 //   written to all W ranks (the outputs are replicated, as after an all-reduce).
 //
-// Execution:
-//   * Rank r owns the contiguous row slab [row_begin, row_end); CTA b of rank r
-//     processes slab rows b, b + grid, ... One row team of T threads per CTA.
-//   * A ring of S shared-memory slots holds, per row, the W partial rows
-//     (read from each rank's memory by cp.async.bulk — unicast TMA copies,
-//     never multicast) and the local residual row, completing on the slot's
-//     mbarrier. The team refills a slot with its row S ahead right after the
-//     slot has been read.
+// Execution (the single-GPU kernel's structure, farq_kernel.cuh, with wider slots):
+//   * Rank r owns the contiguous row slab [row_begin, row_end). A CTA holds
+//     `teams` row teams (named barriers) and a ring of S >= teams slots; CTA-
+//     local slab row n goes to slot n % S and team n % teams, with the slot's
+//     sequence word (release/acquire) guarding against stale mbarrier phases.
+//   * A slot holds a row's W partial rows — read from every rank's memory by
+//     cp.async.bulk (unicast TMA copies, never multicast) — and its local
+//     residual row, completing on the slot's mbarrier. Phase 1 sums the
+//     partials in rank order. At W <= 2 four teams fit (as on one GPU); at
+//     W = 8 a slot is 9 rows and one team fits.
 //   * Outputs are written with plain stores to each rank's buffer (peer
 //     pointers over NVLink, including this rank's own).
 //   * Two cross-rank barriers per CTA, on epoch flags in every rank's signal
@@ -26,8 +28,8 @@
 //     finished with the previous contents of its output buffers) and at the end
 //     (every peer's writes into this rank's outputs are visible before this
 //     kernel completes). CTA b of rank r meets CTA b of every other rank; the
-//     grid is identical on all ranks. Every wait is bounded in time; a wait
-//     that runs out sets the status word and the CTA returns.
+//     launch shape is identical on all ranks. Every wait is bounded in time; a
+//     wait that runs out sets the status word and the CTA returns.
 #pragma once
 
 #include <type_traits>
@@ -50,7 +52,7 @@ struct ArParams {
   const void* gamma;
   int32_t* status;
   int64_t row_begin, row_end;      // this rank's slab
-  int32_t D, nvec, team_threads, stages, world, rank;
+  int32_t D, nvec, team_threads, teams, stages, world, rank;  // stages: ring slots of the CTA
   uint32_t row_bytes;              // D * sizeof(x element)
   int32_t gamma_dtype, nout_dtype, ue8m0;
   uint32_t epoch;
@@ -60,17 +62,19 @@ struct ArParams {
 };
 
 // Shared memory: gamma (fp32, two planes) | S slots of (W + 1) rows |
-// S mbarriers | reduction words.
+// S mbarriers | S sequence words | per team reduction words.
 struct ArLayout {
-  size_t gamma, slots, bars, red, total;
+  size_t gamma, slots, bars, seq, red, total;
 };
-__host__ __device__ inline ArLayout ar_layout(int D, uint32_t row_bytes, int world, int stages) {
+__host__ __device__ inline ArLayout ar_layout(int D, uint32_t row_bytes, int world, int teams,
+                                              int stages) {
   ArLayout L;
   L.gamma = 0;
   L.slots = (size_t)D * sizeof(float);
   L.bars = L.slots + (size_t)stages * (world + 1) * row_bytes;
-  L.red = L.bars + (size_t)stages * sizeof(uint64_t);
-  L.total = L.red + (size_t)kMaxTeamWarps * sizeof(double);
+  L.seq = L.bars + (size_t)stages * sizeof(uint64_t);
+  L.red = L.seq + (size_t)kMaxStages * sizeof(uint32_t);
+  L.total = L.red + (size_t)teams * kMaxTeamWarps * sizeof(double);
   return L;
 }
 
@@ -111,82 +115,66 @@ __device__ __forceinline__ bool ar_barrier(const ArParams& p, int phase, uint32_
 template <typename Tin, int K, int GL, bool E4M3>
 __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_ar_kernel(const ArParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  const ArLayout L = ar_layout(p.D, p.row_bytes, p.world, p.stages);
+  const ArLayout L = ar_layout(p.D, p.row_bytes, p.world, p.teams, p.stages);
   const int T = p.team_threads;
-  const int tt = threadIdx.x;
-  const int lane = tt & 31;
+  const int TEAMS = p.teams;
+  const int team = threadIdx.x / T;
+  const int tt = threadIdx.x - team * T;
+  const int lane = threadIdx.x & 31;
   const int twarp = tt >> 5;
-  const int S = p.stages;
+  const int S = p.stages;  // ring slots of the CTA, S >= TEAMS
   const int W = p.world;
-  const uint32_t slot_bytes = (uint32_t)(W + 1) * p.row_bytes;
+  const uint32_t rb = p.row_bytes;
+  const uint32_t slot_bytes = (uint32_t)(W + 1) * rb;  // W partial rows, then the residual row
+  const uint32_t bar_id = 1u + (uint32_t)team;
   const float4* sg = reinterpret_cast<const float4*>(smem + L.gamma);
   uint8_t* ring = smem + L.slots;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L.bars);
-  double* red = reinterpret_cast<double*>(smem + L.red);
+  uint32_t* seq = reinterpret_cast<uint32_t*>(smem + L.seq);
+  double* my_red = reinterpret_cast<double*>(smem + L.red) + team * kMaxTeamWarps;
   __shared__ int s_fail;
 
+  // CTA-local slab row n (global row row_begin + blockIdx.x + n*grid) sits in
+  // ring slot n % S and is processed by team n % TEAMS.
   const int64_t G = gridDim.x;
   const int64_t slab = p.row_end - p.row_begin;
   const int64_t nrows = blockIdx.x < slab ? (slab - 1 - blockIdx.x) / G + 1 : 0;
   const uint64_t pol = policy_evict_first();
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
-  // Residual rows and gamma are this rank's own data: their loads are issued
-  // before the start barrier. Partials are read only after it.
-  if (tt == 0) {
+  auto fill = [&](int slot, int64_t row) {
+    const uint32_t bar = smem_u32(&bars[slot]);
+    const uint32_t dst = smem_u32(ring + (size_t)slot * slot_bytes);
+    mbar_arrive_expect_tx(bar, slot_bytes);
+#pragma unroll
+    for (int k = 0; k < kMaxWorld; ++k)  // constant indices keep the peer pointers out of memory
+      if (k < W) bulk_load(dst + (uint32_t)k * rb, p.part[k] + row * rb, rb, bar, pol);
+    bulk_load(dst + (uint32_t)W * rb, p.res + row * rb, rb, bar, pol);
+  };
+
+  if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) mbar_init(smem_u32(&bars[s]), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    // Start barrier: every rank's partial is complete and every rank has
+    // finished with the previous contents of its output buffers.
+    // (test-only flag: wait for an epoch no rank signals)
+    s_fail = ar_barrier(p, 0, p.force_timeout ? p.epoch + 0x40000000u : p.epoch) ? 0 : 1;
+    for (int s = 0; s < S; ++s) {
+      seq[s] = (uint32_t)s;
+      if (!s_fail && s < nrows) fill(s, p.row_begin + blockIdx.x + (int64_t)s * G);
+    }
   }
-  auto fill_res = [&](int slot, int64_t row) {
-    const uint32_t bar = smem_u32(&bars[slot]);
-    const uint32_t dst = smem_u32(ring + (size_t)slot * slot_bytes);
-    mbar_arrive_expect_tx(bar, slot_bytes);  // the whole slot: residual + W partials
-    bulk_load(dst + (uint32_t)W * p.row_bytes, p.res + row * p.row_bytes, p.row_bytes, bar, pol);
-  };
-  auto fill_parts = [&](int slot, int64_t row) {
-    const uint32_t bar = smem_u32(&bars[slot]);
-    const uint32_t dst = smem_u32(ring + (size_t)slot * slot_bytes);
-    for (int k = 0; k < W; ++k)
-      bulk_load(dst + (uint32_t)k * p.row_bytes, p.part[k] + row * p.row_bytes, p.row_bytes, bar,
-                pol);
-  };
-  auto fill = [&](int slot, int64_t row) {
-    fill_res(slot, row);
-    fill_parts(slot, row);
-  };
-  if (tt == 0)
-    for (int s = 0; s < S && s < nrows; ++s) fill_res(s, p.row_begin + blockIdx.x + (int64_t)s * G);
-  for (int v = tt; v < p.nvec; v += blockDim.x) {
+  for (int v = threadIdx.x; v < p.nvec; v += blockDim.x) {
     float g[8];
     load_gamma8(p.gamma, v, p.gamma_dtype, g);
     float4* d = reinterpret_cast<float4*>(smem + L.gamma);
     d[v] = make_float4(g[0], g[1], g[2], g[3]);
     d[p.nvec + v] = make_float4(g[4], g[5], g[6], g[7]);
   }
-  // Start barrier: every rank's partial is complete and every rank has
-  // finished with the previous contents of its output buffers.
-  if (tt == 0) {
-    // (test-only flag: wait for an epoch no rank will signal)
-    s_fail = ar_barrier(p, 0, p.force_timeout ? p.epoch + 0x40000000u : p.epoch) ? 0 : 1;
-    if (!s_fail)
-      for (int s = 0; s < S && s < nrows; ++s)
-        fill_parts(s, p.row_begin + blockIdx.x + (int64_t)s * G);
-  }
   __syncthreads();
   if (s_fail) {
-    // drain the residual copies already queued (bounded), then leave
-    if (tt == 0) {
-      if (p.status) atomicExch(p.status, (int)FARQ_ERR_DEVICE_TIMEOUT);
-      for (int s = 0; s < S && s < nrows; ++s) {
-        // the slot's phase expects W more rows that will never be sent:
-        // complete the transaction count with the missing bytes instead
-        asm volatile("mbarrier.complete_tx.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(&bars[s])),
-                     "r"((uint32_t)W * p.row_bytes)
-                     : "memory");
-        (void)mbar_wait_bounded(smem_u32(&bars[s]), 0, p.wait_limit_ns);
-      }
-    }
+    if (threadIdx.x == 0 && p.status) atomicExch(p.status, (int)FARQ_ERR_DEVICE_TIMEOUT);
     return;
   }
 
@@ -196,24 +184,24 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_ar_kernel(const ArPara
   const int xdt = std::is_same<Tin, __nv_bfloat16>::value ? FARQ_DTYPE_BF16 : FARQ_DTYPE_FP16;
   const int groups = p.D / (GL * 8);
   bool failed = false;
-  int64_t consumed = nrows;                       // rows whose copy was waited for
-  int64_t issued = nrows < S ? nrows : (int64_t)S;  // rows whose copy was queued
-  int s = 0;
-  uint32_t parity = 0;
+  int64_t n = team;
+  int s = team % S;
+  uint32_t jf = (uint32_t)(team / S);  // fill count of the slot
 
-  for (int64_t n = 0; n < nrows; ++n) {
+  for (; n < nrows; n += TEAMS) {
     const int64_t row = p.row_begin + blockIdx.x + n * G;
-    const bool ok = mbar_wait_bounded(smem_u32(&bars[s]), parity, p.wait_limit_ns);
-    if (__syncthreads_or(!ok)) {
+    bool ok = seq_wait_bounded(&seq[s], (uint32_t)n, p.wait_limit_ns);
+    ok = ok && mbar_wait_bounded(smem_u32(&bars[s]), jf & 1u, p.wait_limit_ns);
+    if (team_sync_or(bar_id, T, !ok)) {
       if (tt == 0 && p.status) atomicExch(p.status, (int)FARQ_ERR_DEVICE_TIMEOUT);
       failed = true;
-      consumed = n;
       break;
     }
     const uint8_t* slot = ring + (size_t)s * slot_bytes;
-    const uint8_t* sr = slot + (size_t)W * p.row_bytes;
+    const uint8_t* sr = slot + (size_t)W * rb;
 
-    // ---- phase 1: x = sum of partials (rank order), r = x + residual
+    // ---- phase 1: x = sum of the partials in rank order, rounded to the
+    // input dtype (the all-reduced activation); r = x + residual
     float w[K][8];
     float gmax[K];
     double ss0 = 0.0, ss1 = 0.0;
@@ -222,14 +210,13 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_ar_kernel(const ArPara
       const int v = k * T + tt;
       float m = 0.f;
       if (v < nvec) {
-        float a[8], b[8], t[8];
+        float a[8], b[8];
         Unpack<Tin>::run(reinterpret_cast<const uint4*>(slot)[v], a);
         for (int rk = 1; rk < W; ++rk) {
-          Unpack<Tin>::run(reinterpret_cast<const uint4*>(slot + (size_t)rk * p.row_bytes)[v], t);
+          Unpack<Tin>::run(reinterpret_cast<const uint4*>(slot + (size_t)rk * rb)[v], b);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) a[e] += t[e];
+          for (int e = 0; e < 8; ++e) a[e] += b[e];
         }
-        // the all-reduced activation in the input dtype
         const uint4 xr = make_uint4(pack2(a[0], a[1], xdt), pack2(a[2], a[3], xdt),
                                     pack2(a[4], a[5], xdt), pack2(a[6], a[7], xdt));
         Unpack<Tin>::run(xr, a);
@@ -246,7 +233,9 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_ar_kernel(const ArPara
           w[k][e] = a[e] * g[e];
           m = fmaxf(m, fabsf(w[k][e]));
         }
-        for (int rk = 0; rk < W; ++rk) store8(p.rout[rk] + row * p.row_bytes, v, a, xdt);
+#pragma unroll
+        for (int rk = 0; rk < kMaxWorld; ++rk)
+          if (rk < W) store8(p.rout[rk] + row * rb, v, a, xdt);
       } else {
 #pragma unroll
         for (int e = 0; e < 8; ++e) w[k][e] = 0.f;
@@ -258,15 +247,17 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_ar_kernel(const ArPara
     double ss = ss0 + ss1;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (lane == 0) red[twarp] = ss;
-    __syncthreads();
-    if (n + S < nrows) {
-      if (tt == 0) fill(s, row + (int64_t)S * G);
-      ++issued;
+    if (lane == 0) my_red[twarp] = ss;
+    team_sync(bar_id, T);
+
+    // The slot is no longer read: refill it with CTA row n + S.
+    if (tt == 0 && n + S < nrows) {
+      fill(s, row + (int64_t)S * G);
+      seq_release(&seq[s], (uint32_t)(n + S));
     }
 
     double total = 0.0;
-    for (int j = 0; j < tw; ++j) total += red[j];
+    for (int q = 0; q < tw; ++q) total += my_red[q];
     const float inv_rms =
         __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(__double2float_rn(total), (float)p.D), p.eps)));
     const float step = __fdiv_rn(inv_rms, qmax);
@@ -282,10 +273,13 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_ar_kernel(const ArPara
         float nrm[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) nrm[e] = w[k][e] * inv_rms;
-        if (p.nout[0])
-          for (int rk = 0; rk < W; ++rk)
-            store8(p.nout[rk] + row * (int64_t)p.D * (p.nout_dtype == FARQ_DTYPE_FP32 ? 4 : 2), v,
-                   nrm, p.nout_dtype);
+        if (p.nout[0]) {
+#pragma unroll
+          for (int rk = 0; rk < kMaxWorld; ++rk)
+            if (rk < W)
+              store8(p.nout[rk] + row * (int64_t)p.D * (p.nout_dtype == FARQ_DTYPE_FP32 ? 4 : 2),
+                     v, nrm, p.nout_dtype);
+        }
         uint32_t lo, hi;
         if (E4M3) {
           lo = e4m3x2(nrm[0] * isc, nrm[1] * isc) | (e4m3x2(nrm[2] * isc, nrm[3] * isc) << 16);
@@ -296,33 +290,39 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_ar_kernel(const ArPara
           hi = i8(nrm[4] * isc) | (i8(nrm[5] * isc) << 8) | (i8(nrm[6] * isc) << 16) |
                (i8(nrm[7] * isc) << 24);
         }
-        for (int rk = 0; rk < W; ++rk) {
-          st_cs_v2(p.q[rk] + row * (int64_t)p.D + 8 * (int64_t)v, lo, hi);
-          if ((lane & (GL - 1)) == 0) st_cs_f32(p.scale[rk] + row * groups + v / GL, sc);
+#pragma unroll
+        for (int rk = 0; rk < kMaxWorld; ++rk) {
+          if (rk < W) {
+            st_cs_v2(p.q[rk] + row * (int64_t)p.D + 8 * (int64_t)v, lo, hi);
+            if ((lane & (GL - 1)) == 0) st_cs_f32(p.scale[rk] + row * groups + v / GL, sc);
+          }
         }
       }
     }
-    if (++s == S) {
-      s = 0;
-      parity ^= 1u;
+    s += TEAMS;
+    if (s >= S) {
+      s -= S;
+      ++jf;
     }
   }
 
-  if (failed) {
-    // drain the copies still armed for this CTA's slots (bounded), then leave
-    // without the end barrier: a peer did not deliver.
-    __syncthreads();
-    if (tt == 0)
-      for (int64_t j = consumed; j < issued; ++j)
-        (void)mbar_wait_bounded(smem_u32(&bars[j % S]), (uint32_t)((j / S) & 1), p.wait_limit_ns);
+  // After a failed wait: drain every slot's last armed fill (bounded) and
+  // skip the end barrier (a peer did not deliver).
+  if (__syncthreads_or(failed)) {
+    if (threadIdx.x == 0)
+      for (int t = 0; t < S; ++t) {
+        const uint32_t last = ld_acquire(&seq[t]);
+        if ((int64_t)last < nrows)
+          (void)mbar_wait_bounded(smem_u32(&bars[t]), (last / (uint32_t)S) & 1u, p.wait_limit_ns);
+      }
     return;
   }
-  // End barrier: this CTA's stores to every rank are visible system-wide
-  // before it signals; the kernel completes only after every rank's CTA of
-  // the same index has signalled, i.e. after all writes into this rank landed.
-  fence_acq_rel_sys();  // each thread: its stores to every rank before the signal
+  // End barrier: every thread's stores to every rank are ordered before the
+  // signal; the kernel completes only after every rank's CTA of the same
+  // index has signalled, i.e. after all writes into this rank landed.
+  fence_acq_rel_sys();
   __syncthreads();
-  if (tt == 0) {
+  if (threadIdx.x == 0) {
     if (!ar_barrier(p, 1, p.epoch) && p.status) atomicExch(p.status, (int)FARQ_ERR_DEVICE_TIMEOUT);
   }
 }
