@@ -219,7 +219,8 @@ const char* farq_strerror(int status) {
     case FARQ_ERR_ALIGNMENT: return "misaligned pointer or row stride (16-byte rows required)";
     case FARQ_ERR_UNSUPPORTED: return "hidden size or tuning choice outside the supported range (D <= 16384)";
     case FARQ_ERR_CUDA: return "a CUDA runtime call failed";
-    case FARQ_ERR_BAD_ARGS_SIZE: return "farq_args_t size mismatch (header and library differ)";
+    case FARQ_ERR_BAD_ARGS_SIZE:
+      return "argument struct size mismatch (header and library differ) or reserved field not 0";
     case FARQ_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait ran out";
     case FARQ_ERR_NOALLOC_TOO_LARGE:
       return "call needs more than the 64 MiB staging array of farq_launch_host_noalloc; split the rows";
@@ -251,7 +252,7 @@ int farq_plan(int64_t M, int64_t D, int32_t group_size, int32_t x_dtype, int32_t
 
 int farq_launch(const farq_args_t* a, void* stream) {
   if (!a) return FARQ_ERR_NULL_POINTER;
-  if (a->struct_size != sizeof(farq_args_t)) return FARQ_ERR_BAD_ARGS_SIZE;
+  if (a->struct_size != sizeof(farq_args_t) || a->reserved0 != 0) return FARQ_ERR_BAD_ARGS_SIZE;
   const int64_t M = a->M, D = a->D;
   const int G = a->group_size;
   int st = check_shape(M, D, G);
@@ -355,7 +356,7 @@ int farq_launch(const farq_args_t* a, void* stream) {
 
 int farq_ar_launch(const farq_ar_args_t* a, void* stream) {
   if (!a) return FARQ_ERR_NULL_POINTER;
-  if (a->struct_size != sizeof(farq_ar_args_t)) return FARQ_ERR_BAD_ARGS_SIZE;
+  if (a->struct_size != sizeof(farq_ar_args_t) || a->reserved0 != 0) return FARQ_ERR_BAD_ARGS_SIZE;
   const int64_t M = a->M, D = a->D;
   const int G = a->group_size, W = a->world;
   int st = check_shape(M, D, G);

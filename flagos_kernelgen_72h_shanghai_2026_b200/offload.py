@@ -113,9 +113,10 @@ def fused_add_rmsnorm_group_quant_host(x, residual, gamma, residual_out, norm_ou
             x_scale[a:b].copy_(sl["s"][:n], non_blocking=True)
             pipe.ev_out[k].record(pipe.d2h)
         pipe.used[k] = True
-        # the staging slot may not be reused by the caller's allocator meanwhile
-        for t in (g,):
-            t.record_stream(pipe.comp)
+    if g is not gamma:
+        # gamma was copied to the device for this call: keep that copy alive
+        # until the kernels on the pipeline's compute stream have read it
+        g.record_stream(pipe.comp)
     last = torch.cuda.Event()
     last.record(pipe.d2h)
     caller.wait_event(last)

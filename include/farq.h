@@ -74,7 +74,8 @@ enum farq_status {
     FARQ_ERR_ALIGNMENT = 5,        /* row base or row stride not 16-B aligned */
     FARQ_ERR_UNSUPPORTED = 6,      /* D or a tuning choice out of range      */
     FARQ_ERR_CUDA = 7,             /* a CUDA runtime call failed             */
-    FARQ_ERR_BAD_ARGS_SIZE = 8,    /* struct_size does not match this build  */
+    FARQ_ERR_BAD_ARGS_SIZE = 8,    /* struct_size does not match this build,
+                                      or a reserved field is not 0          */
     FARQ_ERR_DEVICE_TIMEOUT = 9,   /* a bounded device wait ran out          */
     FARQ_ERR_NOALLOC_TOO_LARGE = 10 /* call needs more than the 64 MiB staging
                                        array of farq_launch_host_noalloc     */

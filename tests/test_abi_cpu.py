@@ -46,6 +46,11 @@ def test_struct_layout_matches_header(lib):
     assert lib.farq_launch(ctypes.byref(a), None) == _lib.ERR_BAD_ARGS_SIZE
 
 
+def test_reserved_field_must_be_zero(lib):
+    a = _args(reserved0=1)
+    assert lib.farq_launch(ctypes.byref(a), None) == _lib.ERR_BAD_ARGS_SIZE
+
+
 def test_version_and_limits(lib):
     assert lib.farq_abi_version() == _lib.ABI_VERSION
     assert lib.farq_max_hidden() == 16384
