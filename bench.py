@@ -131,9 +131,12 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ CPU arm
-def cpu_sample(w, steps: int, warmup: int, budget_s: float):
+def cpu_sample(w, steps: int, warmup: int, budget_s: float, min_rows: int = 1):
     """Time the CPU restatement (oracle port) on a bounded row sample of ``w``
-    with all host threads. Returns (GB/s, seconds per step, rows, cores)."""
+    with all host threads: rows per step sized so that steps + warmup calls
+    take about ``budget_s`` seconds, but never fewer than ``min_rows`` (small
+    samples would measure per-call overhead rather than throughput).
+    Returns (GB/s, seconds per step, rows, cores)."""
     from oracle.farq_oracle import fused_add_rmsnorm_group_quant_ref
     cores = len(os.sched_getaffinity(0))
     torch.set_num_threads(cores)
@@ -144,7 +147,7 @@ def cpu_sample(w, steps: int, warmup: int, budget_s: float):
     fused_add_rmsnorm_group_quant_ref(x, r, g, w.eps, w.group_size, mode, w.ue8m0)
     per_row = (time.perf_counter() - t0) / probe_rows
     rows = int(budget_s / max(1, steps + warmup) / max(per_row, 1e-9))
-    rows = max(1, min(w.M, rows))
+    rows = max(min_rows, min(w.M, rows))
     x, r, g = make_inputs(w.with_rows(rows))
     for _ in range(warmup):
         fused_add_rmsnorm_group_quant_ref(x, r, g, w.eps, w.group_size, mode, w.ue8m0)
@@ -159,7 +162,8 @@ def cpu_sample(w, steps: int, warmup: int, budget_s: float):
 def run_reference_arm(args, w, rank, world):
     if rank != 0:
         return
-    gbs, dt, rows, cores = cpu_sample(w, args.steps, args.warmup, budget_s=args.cpu_budget)
+    gbs, dt, rows, cores = cpu_sample(w, args.steps, args.warmup, budget_s=args.ref_budget,
+                                      min_rows=16)
     sample = f"{rows} of {w.M} rows of {w.name} per step, oracle port, fp32 torch CPU"
     line = {
         "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "impl": "reference",
@@ -425,6 +429,8 @@ def main():
     ap.add_argument("--e2e-chunk-rows", type=int, default=512)
     ap.add_argument("--cpu-budget", type=float, default=12.0,
                     help="seconds of CPU work for the CPU baseline sample")
+    ap.add_argument("--ref-budget", type=float, default=90.0,
+                    help="seconds of CPU work for the whole --impl reference run")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
