@@ -9,8 +9,8 @@ batch of synthetic input already resident in HBM.
 
 Under torchrun (N > 1) every rank runs its own shard of rows; rank 0 prints
 one JSON line. ``--impl reference`` times the CPU restatement of the
-reference's math (the reference itself is Triton-only and ships no CPU code)
-on the host cores, on rank 0 only.
+reference's math (the reference itself is Triton-only and ships no CPU code;
+oracle/farq_oracle.c, OpenMP) on the host cores, on rank 0 only.
 """
 from __future__ import annotations
 
@@ -132,28 +132,34 @@ class ClockSampler:
 
 # ------------------------------------------------------------------ CPU arm
 def cpu_sample(w, steps: int, warmup: int, budget_s: float, min_rows: int = 1):
-    """Time the CPU restatement (oracle port) on a bounded row sample of ``w``
-    with all host threads: rows per step sized so that steps + warmup calls
-    take about ``budget_s`` seconds, but never fewer than ``min_rows`` (small
-    samples would measure per-call overhead rather than throughput).
+    """Time the plain-C restatement of the reference math (oracle/farq_oracle.c,
+    OpenMP over rows, all host threads) on a bounded row sample of ``w``:
+    rows per step sized so that steps + warmup calls take about ``budget_s``
+    seconds, but never fewer than ``min_rows`` (small samples would measure
+    per-call overhead rather than throughput).
     Returns (GB/s, seconds per step, rows, cores)."""
-    from oracle.farq_oracle import fused_add_rmsnorm_group_quant_ref
+    from oracle.c_oracle import fused_add_rmsnorm_group_quant_c
     cores = len(os.sched_getaffinity(0))
-    torch.set_num_threads(cores)
     mode = "e4m3" if w.q_dtype == torch.float8_e4m3fn else "int8"
-    probe_rows = min(64, w.M)
+
+    def call(x, r, g):
+        fused_add_rmsnorm_group_quant_c(x, r, g, w.eps, w.group_size, mode, w.ue8m0,
+                                        write_norm=False, threads=cores)
+
+    probe_rows = min(256, w.M)
     x, r, g = make_inputs(w.with_rows(probe_rows))
+    call(x, r, g)
     t0 = time.perf_counter()
-    fused_add_rmsnorm_group_quant_ref(x, r, g, w.eps, w.group_size, mode, w.ue8m0)
+    call(x, r, g)
     per_row = (time.perf_counter() - t0) / probe_rows
     rows = int(budget_s / max(1, steps + warmup) / max(per_row, 1e-9))
     rows = max(min_rows, min(w.M, rows))
     x, r, g = make_inputs(w.with_rows(rows))
     for _ in range(warmup):
-        fused_add_rmsnorm_group_quant_ref(x, r, g, w.eps, w.group_size, mode, w.ue8m0)
+        call(x, r, g)
     t0 = time.perf_counter()
     for _ in range(steps):
-        fused_add_rmsnorm_group_quant_ref(x, r, g, w.eps, w.group_size, mode, w.ue8m0)
+        call(x, r, g)
     dt = (time.perf_counter() - t0) / steps
     b = bytes_per_call(rows, w.D, w.group_size)
     return b / dt / 1e9, dt, rows, cores
@@ -164,7 +170,8 @@ def run_reference_arm(args, w, rank, world):
         return
     gbs, dt, rows, cores = cpu_sample(w, args.steps, args.warmup, budget_s=args.ref_budget,
                                       min_rows=16)
-    sample = f"{rows} of {w.M} rows of {w.name} per step, oracle port, fp32 torch CPU"
+    sample = (f"{rows} of {w.M} rows of {w.name} per step, plain-C port of the reference math "
+              f"(oracle/farq_oracle.c, OpenMP, {cores} threads)")
     line = {
         "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "impl": "reference",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -277,8 +284,8 @@ def run_ours(args, w, rank, world, local):
     if rank == 0 and world == 1 and not args.no_cpu:
         gbs, dt, srows, cores = cpu_sample(w, 3, 1, budget_s=args.cpu_budget)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
-               "sample": f"{srows} rows of {w.name} per call, oracle port (fp32 torch CPU), "
-                         f"3 timed calls"}
+               "sample": f"{srows} rows of {w.name} per call, plain-C port of the reference math "
+                         f"(oracle/farq_oracle.c, OpenMP, {cores} threads), 3 timed calls"}
     if pg:
         pg.destroy_process_group()
     if rank != 0:

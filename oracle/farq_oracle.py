@@ -1,8 +1,9 @@
 """CPU oracle for fused residual-add + RMSNorm + per-token group quantisation.
 
-TEST INFRASTRUCTURE ONLY. This module is the checker for the CUDA path and
-the timed CPU baseline ("port" of the reference's math); it is imported only
-by tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg. The
+TEST INFRASTRUCTURE ONLY. This module is the checker for the CUDA path; it is
+imported only by tests/ and __graft_entry__.smoke(). (The timed CPU baseline
+is the plain-C restatement in farq_oracle.c, which matches this module bit
+for bit.) The
 product path (flagos_kernelgen_72h_shanghai_2026_b200) never calls it.
 
 It restates, in vectorised fp32 torch-on-CPU code, the per-row arithmetic of

@@ -89,3 +89,32 @@ def test_e4m3_mode_saturates_and_round_trips():
     assert q.view(torch.float8_e4m3fn).float().abs().amax().item() == 448.0
     err = (deq - norm).abs()
     assert bool((err <= norm.abs() * 0.0625 + s[:, :, None] * 2 ** -9 + norm.abs() * 2 ** -8).all())
+
+
+@pytest.mark.parametrize("cfg", ["bf16_g128", "fp16_g64_ue8m0", "outliers", "zero_row", "small_g"])
+@pytest.mark.parametrize("mode", ["int8", "e4m3"])
+def test_c_oracle_matches_torch_oracle_bit_for_bit(cfg, mode):
+    """Two independent CPU restatements (torch and plain C) agree exactly."""
+    from oracle.c_oracle import fused_add_rmsnorm_group_quant_c
+    from flagos_kernelgen_72h_shanghai_2026_b200.workloads import Workload, make_inputs
+    ue8m0 = False
+    if cfg == "bf16_g128":
+        w = Workload("c1", 64, 7168, res_std=2.0, seed=61)
+    elif cfg == "fp16_g64_ue8m0":
+        w = Workload("c2", 48, 5120, dtype=torch.float16, group_size=64, eps=1e-5, seed=62)
+        ue8m0 = True
+    elif cfg == "outliers":
+        w = Workload("c3", 100, 7168, outlier_channels=8, outlier_row_frac=0.05, seed=63)
+    elif cfg == "zero_row":
+        w = Workload("c4", 5, 8192, group_size=256, seed=64)
+    else:
+        w = Workload("c5", 33, 1024, group_size=8, seed=65)
+    x, r, g = make_inputs(w)
+    if cfg == "zero_row":
+        x[2] = 0
+        r[2] = 0
+    ref = fused_add_rmsnorm_group_quant_ref(x, r, g, w.eps, w.group_size, mode, ue8m0)
+    got = fused_add_rmsnorm_group_quant_c(x, r, g, w.eps, w.group_size, mode, ue8m0, threads=4)
+    names = ("residual_out", "norm_out", "q", "scale")
+    for name, a, b in zip(names, got, ref):
+        assert torch.equal(a.contiguous().view(torch.uint8), b.contiguous().view(torch.uint8)), name
