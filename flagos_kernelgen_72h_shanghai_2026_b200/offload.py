@@ -47,7 +47,8 @@ class _Pipeline:
         self.used = [False] * _SLOTS
 
 
-_PIPES: dict = {}
+_PIPES: dict = {}     # (device, shape, dtypes) -> _Pipeline, least recently used first
+_MAX_PIPES = 4        # staging buffers kept alive for at most this many shapes
 
 
 def fused_add_rmsnorm_group_quant_host(x, residual, gamma, residual_out, norm_out, x_q, x_scale,
@@ -75,10 +76,14 @@ def fused_add_rmsnorm_group_quant_host(x, residual, gamma, residual_out, norm_ou
     groups = D // int(group_size) if group_size else 0
     key = (device, chunk, D, groups, x.dtype, residual_out.dtype,
            norm_out.dtype if write_norm else None, x_q.dtype)
-    pipe = _PIPES.get(key)
+    pipe = _PIPES.pop(key, None)
     if pipe is None:
-        pipe = _PIPES[key] = _Pipeline(device, chunk, D, groups, x.dtype, residual_out.dtype,
-                                       norm_out.dtype if write_norm else None, x_q.dtype)
+        if len(_PIPES) >= _MAX_PIPES:
+            old = _PIPES.pop(next(iter(_PIPES)))
+            old.d2h.synchronize()  # its last copies have finished with its buffers
+        pipe = _Pipeline(device, chunk, D, groups, x.dtype, residual_out.dtype,
+                         norm_out.dtype if write_norm else None, x_q.dtype)
+    _PIPES[key] = pipe  # most recently used last
     g = gamma.to(device, non_blocking=True) if gamma.device != device else gamma
     caller = torch.cuda.current_stream(device)
     ev_start = torch.cuda.Event()
