@@ -7,7 +7,6 @@ NVIDIA device (src/task01_fused_add_rmsnorm_group_quant.py:1772-1817, :1656-1727
 from __future__ import annotations
 
 import hashlib
-from dataclasses import replace
 
 import torch
 

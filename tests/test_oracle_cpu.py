@@ -64,13 +64,11 @@ def test_e4m3_encoder_grid_midpoints_and_saturation():
     mids = (pos[:-1] + pos[1:]) / 2
     out = e4m3_rne_sat(mids)
     lo_codes = pos[:-1].to(torch.float8_e4m3fn).view(torch.uint8)
-    hi_codes = pos[1:].to(torch.float8_e4m3fn).view(torch.uint8)
     even = torch.where(lo_codes % 2 == 0, pos[:-1], pos[1:])
     assert torch.equal(out, even)
     sat = e4m3_rne_sat(torch.tensor([449.0, 464.0, 500.0, 1e30, float("inf"), -1e9]))
     assert sat.tolist() == [448.0, 448.0, 448.0, 448.0, 448.0, -448.0]
     assert torch.isnan(e4m3_rne_sat(torch.tensor([float("nan")]))).all()
-    del hi_codes
 
 
 def test_pow2_ceil():
