@@ -35,8 +35,8 @@
 //     flips a group-maximum element (which sits on ±QMAX mathematically)
 //     between two codes, on ~1/(2G) of all elements.
 //   * Launched with programmatic stream serialisation: the next call's CTAs
-//     launch and set up while this one drains, and wait (griddepcontrol)
-//     before their first global-memory access.
+//     launch, set up and prefetch their first rows into L2 while this one
+//     drains, and wait (griddepcontrol) before their first global-memory read.
 //   * Every device-side wait is bounded; a wait that runs out sets the
 //     caller's status word, and the CTA drains its copies and returns.
 #pragma once
@@ -153,6 +153,10 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
       " [%0], [%1], %2, [%3], %4;" ::"r"(dst),
       "l"(src), "r"(bytes), "r"(bar), "l"(pol)
       : "memory");
+}
+// Prefetch `bytes` (multiple of 16, 16-byte aligned) of global memory into L2.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 // Release store / acquire load of a shared-memory word (slot sequence numbers).
 __device__ __forceinline__ void seq_release(uint32_t* p, uint32_t v) {
@@ -319,6 +323,18 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_rows_kernel(const Para
   // previous kernel in the stream was still draining. Wait for it to finish
   // (and its writes to be visible) before touching global memory, and let the
   // next launch begin its own set-up as early as possible.
+  // While the previous kernel drains, warm L2 with this CTA's first rows and
+  // gamma. A bulk L2 prefetch only moves lines into the device's L2, the point
+  // of coherence for every writer, so data the previous kernel still writes
+  // lands there too and the reads after the wait below see it.
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S && s < nrows; ++s) {
+      const int64_t row = blockIdx.x + (int64_t)s * G;
+      bulk_prefetch_l2(p.x + row * p.sx, p.row_bytes);
+      bulk_prefetch_l2(p.res + row * p.sr, p.row_bytes);
+    }
+    bulk_prefetch_l2(p.gamma, (uint32_t)p.nvec * (p.gamma_dtype == FARQ_DTYPE_FP32 ? 32u : 16u));
+  }
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
