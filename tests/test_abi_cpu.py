@@ -133,3 +133,20 @@ def test_ar_entry_validation_codes(lib):
     assert lib.farq_ar_launch(ctypes.byref(a), None) == _lib.ERR_NULL_POINTER
     a.M = 0
     assert lib.farq_ar_launch(ctypes.byref(a), None) == _lib.OK
+
+
+def test_noalloc_entry_validation_before_any_device_call(lib):
+    f = lib.farq_launch_host_noalloc
+    f.argtypes = [ctypes.POINTER(_lib.FarqArgs), ctypes.c_void_p]
+    f.restype = ctypes.c_int
+    assert f(None, None) == _lib.ERR_NULL_POINTER
+    a = _args(struct_size=4)
+    assert f(ctypes.byref(a), None) == _lib.ERR_BAD_ARGS_SIZE
+    assert f(ctypes.byref(_args(group_size=100)), None) == _lib.ERR_BAD_SHAPE
+    assert f(ctypes.byref(_args(x_row_stride=2048)), None) == _lib.ERR_BAD_SHAPE  # host tensors contiguous
+    assert f(ctypes.byref(_args()), None) == _lib.ERR_NULL_POINTER
+    # 100k rows x 7168 needs far more than the 64 MiB staging array: rejected up front
+    big = _args(M=100000, D=7168, x=0x1000, residual=0x2000, gamma=0x3000, residual_out=0x4000,
+                x_q=0x5000, x_scale=0x6000)
+    assert f(ctypes.byref(big), None) == _lib.ERR_NOALLOC_TOO_LARGE
+    assert f(ctypes.byref(_args(M=0)), None) == _lib.OK
