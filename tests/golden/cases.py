@@ -34,6 +34,12 @@ CASES = {
         Workload("g6", 513, 4096, dtype=torch.float16, group_size=256, q_dtype=torch.int8,
                  seed=5), (),
         "_nvidia_parallel_row_group_streaming_kernel"),
+    "segmented_130x8192_g256_4seg": (
+        Workload("g8", 130, 8192, group_size=256, q_dtype=torch.int8, res_std=2.0, seed=7), (),
+        "_preweighted_segmented_streaming_kernel"),
+    "rowgroup_512x6144_g128_3seg": (
+        Workload("g9", 512, 6144, q_dtype=torch.int8, seed=8), (),
+        "_nvidia_parallel_row_group_streaming_kernel"),
     "full_row_1x4096_g128": (
         Workload("g7", 1, 4096, q_dtype=torch.int8, seed=6), (), "_preweighted_full_row_kernel"),
 }
