@@ -5,10 +5,13 @@ T x 7168, on 1/2/4/8 GPUs (one process per GPU, rows sharded, no collective
 inside the timed region). One step = one call of the operator over one
 batch of synthetic input already resident in HBM.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 5] [--impl ours|reference]
 
-Under torchrun (N > 1) every rank runs its own shard of rows; rank 0 prints
-one JSON line. ``--impl reference`` times the CPU restatement of the
+Default workload: config 5, 262144 x 7168 bf16 rows split evenly over the N
+GPUs (strong scaling, no collective in the timed region); the DeepSeek-V3
+4096 x 7168 call on one GPU (config 2) is timed as well and reported beside
+it. Under torchrun (N > 1) every rank runs its own slab of rows; rank 0
+prints one JSON line. ``--impl reference`` times the CPU restatement of the
 reference's math (the reference itself is Triton-only and ships no CPU code;
 oracle/farq_oracle.c, OpenMP) on the host cores, on rank 0 only.
 """
@@ -68,20 +71,28 @@ def load_peak() -> tuple[float, str]:
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def profiled_traffic(workload: str) -> float | None:
-    """DRAM bytes per launch from the committed ncu summary of this workload, if any."""
-    for f in sorted((ROOT / "profiles").glob("*.md")):
+def profiled_traffic_per_row(D: int) -> float | None:
+    """DRAM read + write bytes per row of one launch of the row kernel at
+    hidden size D, from the committed ncu summary of that kernel (the
+    ``traffic_bytes_per_row`` line of a ``profiles/farq_rows_kernel_*`` file
+    whose ``hidden: D`` matches). The benchmark's full launches are too large
+    to capture under ncu; DRAM traffic of this kernel grows in proportion to
+    the rows it processes, so the bench scales this figure by its rows."""
+    for f in sorted((ROOT / "profiles").glob("farq_rows_kernel_*.md")):
         text = f.read_text()
-        if f"workload: {workload}" not in text:
+        if not re.search(rf"^hidden: {D}$", text, flags=re.M):
             continue
-        m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", text)
+        m = re.search(r"traffic_bytes_per_row:\s*([0-9.eE+]+)", text)
         if m:
             return float(m.group(1))
     return None
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason samples while the timed region runs."""
+    """nvidia-smi clock / throttle-reason samples while the GPU is under load.
+
+    Started before the warm-up, so that nvidia-smi is already sampling when
+    the timed region begins (no idle gap is inserted for it)."""
 
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
@@ -93,8 +104,7 @@ class ClockSampler:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={SMI_FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100", "-i", str(self.idx)], stdout=self.fh, stderr=subprocess.DEVNULL)
-            time.sleep(0.3)
+                 "-lms", "50", "-i", str(self.idx)], stdout=self.fh, stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
         return self
@@ -128,6 +138,30 @@ class ClockSampler:
         self.path.unlink(missing_ok=True)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
                 "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def line_config(w, world: int, scaling: str) -> dict:
+    """`config` of the JSON line; identical for the repo arm and the reference
+    arm at the same workload and N, so the driver can pair them."""
+    start, stop = shard_rows(w.M, world, 0) if scaling == "strong" else (0, w.M)
+    return {"workload": w.name, "M": w.M if scaling == "strong" else w.M * world,
+            "M_per_gpu": stop - start, "D": w.D, "group_size": w.group_size,
+            "io_dtype": "bf16" if w.dtype == torch.bfloat16 else "fp16",
+            "q_dtype": str(w.q_dtype).replace("torch.", ""), "ue8m0": w.ue8m0,
+            "norm_out": False,
+            "bytes_per_call": job_bytes(w, world, scaling),
+            "parallelism": f"rows sharded over {world} GPU(s), no collective"}
+
+
+def job_bytes(w, world: int, scaling: str) -> int:
+    """Algorithmic bytes of one step of the whole job: every row once, plus
+    one gamma read per GPU."""
+    total_rows = w.M if scaling == "strong" else w.M * world
+    return bytes_per_call(total_rows, w.D, w.group_size) + (world - 1) * 2 * w.D
+
+
+# Both arms compute in fp32 (fp64 sum of squares on the GPU) on 2-byte inputs.
+LINE_DTYPE = "fp32"
 
 
 # ------------------------------------------------------------------ CPU arm
@@ -177,9 +211,9 @@ def run_reference_arm(args, w, rank, world):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dt * 1e3, "ms_per_full_call_extrapolated": dt * 1e3 * (w.M / rows),
         "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-        "config": {"workload": w.name, "M": w.M, "D": w.D, "group_size": w.group_size,
-                   "q_dtype": str(w.q_dtype).replace("torch.", ""), "rows_per_step": rows},
+        "scaling": args.scaling, "vs_baseline": None, "dtype": LINE_DTYPE, "data": "synthetic",
+        "config": line_config(w, world, args.scaling),
+        "rows_per_step": rows,
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
@@ -189,6 +223,55 @@ def run_reference_arm(args, w, rank, world):
 
 
 # ------------------------------------------------------------------ GPU arm
+def rotating_sets(w, rows, start, rank, dev):
+    """Input/output sets for ``rows`` rows, enough of them that consecutive
+    steps never find their inputs in the 126 MB L2 (one set suffices when a
+    set is itself several times larger than L2)."""
+    per_set = bytes_per_call(rows, w.D, w.group_size)
+    nsets = 1 if per_set >= 3 * L2_BYTES else min(64, max(2, -(-(3 * L2_BYTES) // per_set)))
+    x0, r0, g = make_inputs(w, device=dev, row_start=start, row_stop=start + rows,
+                            seed_offset=rank)
+    sets = []
+    for i in range(nsets):
+        x = x0 if i == 0 else x0.roll(i, dims=0).contiguous()
+        r = r0 if i == 0 else r0.roll(i, dims=0).contiguous()
+        sets.append((x, r) + alloc_outputs(w, rows, dev))
+    return sets, g, per_set
+
+
+def timed_steps(step, K, W, stream, dev, pg, min_warm_s):
+    """W warm-up steps (extended until the GPU has been busy for at least
+    ``min_warm_s``, so clocks and memory are at their loaded state), then
+    exactly K steps between two CUDA events, with a barrier and a device
+    synchronize on both sides. Returns (total ms, warm-up steps run)."""
+    w0 = torch.cuda.Event(enable_timing=True)
+    w1 = torch.cuda.Event(enable_timing=True)
+    w0.record(stream)
+    for i in range(W):
+        step(i)
+    w1.record(stream)
+    torch.cuda.synchronize(dev)
+    warm_ms = w0.elapsed_time(w1)
+    extra = 0
+    if warm_ms < min_warm_s * 1e3:
+        extra = int((min_warm_s * 1e3 - warm_ms) / max(warm_ms / W, 1e-3)) + 1
+        for i in range(extra):
+            step(W + i)
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize(dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(K):
+        step(i)
+    t1.record(stream)
+    torch.cuda.synchronize(dev)
+    if pg:
+        pg.barrier()
+    return t0.elapsed_time(t1), W + extra
+
+
 def run_ours(args, w, rank, world, local):
     from flagos_kernelgen_72h_shanghai_2026_b200 import fused_add_rmsnorm_group_quant
     from flagos_kernelgen_72h_shanghai_2026_b200._build import build_lib
@@ -206,41 +289,17 @@ def run_ours(args, w, rank, world, local):
     else:
         start, stop = 0, w.M
     rows = stop - start
-    per_set = bytes_per_call(rows, w.D, w.group_size)
-    nsets = max(2, -(-(3 * L2_BYTES) // per_set)) if per_set < 3 * L2_BYTES else 1
-    nsets = min(nsets, 64)
-    x0, r0, g = make_inputs(w, device=dev, row_start=start, row_stop=stop, seed_offset=rank)
-    sets = []
-    for i in range(nsets):
-        x = x0 if i == 0 else x0.roll(i, dims=0).contiguous()
-        r = r0 if i == 0 else r0.roll(i, dims=0).contiguous()
-        sets.append((x, r) + alloc_outputs(w, rows, dev))
-    eps, G = w.eps, w.group_size
+    sets, g, per_set = rotating_sets(w, rows, start, rank, dev)
+    nsets = len(sets)
+    stream = torch.cuda.current_stream(dev)
 
     def step(i):
         x, r, ro, no, q, s = sets[i % nsets]
-        fused_add_rmsnorm_group_quant(x, r, g, ro, no, q, s, eps, G, ue8m0=w.ue8m0)
-
-    stream = torch.cuda.current_stream(dev)
-    for i in range(args.warmup):
-        step(i)
-    torch.cuda.synchronize(dev)
+        fused_add_rmsnorm_group_quant(x, r, g, ro, no, q, s, w.eps, w.group_size, ue8m0=w.ue8m0)
 
     K = args.steps
-    t_begin = torch.cuda.Event(enable_timing=True)
-    t_end = torch.cuda.Event(enable_timing=True)
-    if pg:
-        pg.barrier()
-    torch.cuda.synchronize(dev)
     with ClockSampler(smi_index(local)) as clocks:
-        t_begin.record(stream)
-        for i in range(K):
-            step(i)
-        t_end.record(stream)
-        torch.cuda.synchronize(dev)
-    if pg:
-        pg.barrier()
-    total_ms = t_begin.elapsed_time(t_end)
+        total_ms, warm_run = timed_steps(step, K, args.warmup, stream, dev, pg, args.min_warm_s)
     # Each step is exactly one launch of the operator's kernel, so the
     # kernel's average duration over the timed region is total / K.
     kern_ms = total_ms / K
@@ -256,29 +315,54 @@ def run_ours(args, w, rank, world, local):
         ends[i].record(stream)
     torch.cuda.synchronize(dev)
     iso_ms = sum(a.elapsed_time(b) for a, b in zip(starts, ends)) / n_iso
+    del sets, step
+
+    # ---- the DeepSeek-V3 shape (config 2, 4096 x 7168) on every GPU, per GPU
+    dsv3 = None
+    if not args.no_dsv3 and w.name != CONFIGS[2].name:
+        w2 = CONFIGS[2]
+        sets2, g2, per2 = rotating_sets(w2, w2.M, 0, rank, dev)
+
+        def step2(i):
+            x, r, ro, no, q, s = sets2[i % len(sets2)]
+            fused_add_rmsnorm_group_quant(x, r, g2, ro, no, q, s, w2.eps, w2.group_size)
+
+        k2 = max(K, 200)
+        ms2, warm2 = timed_steps(step2, k2, args.warmup, stream, dev, pg, args.min_warm_s)
+        dsv3 = {"workload": w2.name, "M_per_gpu": w2.M, "steps": k2, "warmup": warm2,
+                "us_per_call": ms2 / k2 * 1e3, "bytes_per_call": per2}
+        del sets2, step2
 
     # ---- end to end: pinned host inputs -> device -> operator -> host outputs
     e2e = run_e2e(args, w, rows, dev, g, start, rank, pg)
 
-    times = torch.tensor([total_ms, kern_ms, iso_ms], dtype=torch.float64, device=dev)
+    times = torch.tensor([total_ms, kern_ms, iso_ms, e2e["ms"],
+                          dsv3["us_per_call"] if dsv3 else 0.0], dtype=torch.float64, device=dev)
     if pg:
         pg.all_reduce(times, op=pg.ReduceOp.MAX)
-        e2e_t = torch.tensor([e2e["ms"]], dtype=torch.float64, device=dev)
-        pg.all_reduce(e2e_t, op=pg.ReduceOp.MAX)
-        e2e["ms"] = float(e2e_t.item())
         clk_all = [None] * world
         pg.all_gather_object(clk_all, clk)
     else:
         clk_all = [clk]
-    total_ms, kern_ms, iso_ms = float(times[0]), float(times[1]), float(times[2])
+    total_ms, kern_ms, iso_ms, e2e_ms = (float(times[i]) for i in range(4))
     ms_per_step = total_ms / K
-    total_rows = rows * world if args.scaling == "weak" else w.M
-    job_bytes = bytes_per_call(total_rows, w.D, w.group_size) + (world - 1) * 2 * w.D
-    value = job_bytes / (ms_per_step * 1e-3) / 1e9
-    kernel_bytes = per_set
+    jb = job_bytes(w, world, args.scaling)
+    value = jb / (ms_per_step * 1e-3) / 1e9
+    # per-launch figures of the slowest rank: its slab is the largest one
+    if args.scaling == "strong":
+        a, b = shard_rows(w.M, world, world - 1)
+        launch_rows = b - a
+    else:
+        launch_rows = rows
+    kernel_bytes = bytes_per_call(launch_rows, w.D, w.group_size)
     achieved = kernel_bytes / (kern_ms * 1e-3) / 1e9
     peak, peak_kind = load_peak()
-    e2e_gbs = job_bytes / (e2e["ms"] * 1e-3) / 1e9
+    e2e_gbs = jb / (e2e_ms * 1e-3) / 1e9
+    if dsv3:
+        dsv3["us_per_call"] = float(times[4])  # max over ranks
+        dsv3["gbs_per_gpu"] = round(dsv3["bytes_per_call"] / (dsv3["us_per_call"] * 1e-6) / 1e9, 2)
+        dsv3["frac_of_peak"] = round(dsv3["gbs_per_gpu"] / peak, 4)
+        dsv3["peak_kind"] = peak_kind
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -291,44 +375,52 @@ def run_ours(args, w, rank, world, local):
     if rank != 0:
         return
     sm = [c["sm_mhz"] for c in clk_all if c["sm_mhz"]]
+    cfg = line_config(w, world, args.scaling)
+    traffic_row = profiled_traffic_per_row(w.D)
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
-        "steps": K, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "steps": K, "warmup": warm_run, "ms_per_step": ms_per_step,
         "us_per_call": kern_ms * 1e3, "us_per_call_isolated": iso_ms * 1e3,
         "higher_is_better": True, "scaling": args.scaling,
-        "vs_baseline": None, "dtype": "bf16" if w.dtype == torch.bfloat16 else "fp16",
+        "vs_baseline": None, "dtype": LINE_DTYPE,
         "data": "synthetic (seeded torch.randn on device)",
-        "config": {"workload": w.name, "M_per_gpu": rows, "D": w.D, "group_size": w.group_size,
-                   "q_dtype": str(w.q_dtype).replace("torch.", ""), "ue8m0": w.ue8m0,
-                   "norm_out": False, "bytes_per_call": kernel_bytes,
-                   "l2": f"rotating {nsets} input/output sets "
-                         f"({nsets * per_set / 1e6:.0f} MB > {L2_BYTES / 1e6:.0f} MB L2)",
-                   "parallelism": f"rows sharded over {world} GPU(s), no collective"},
+        "config": cfg,
+        "l2": (f"inputs larger than L2: {nsets} rotating input/output set(s) of "
+               f"{per_set / 1e6:.0f} MB per GPU (L2 {L2_BYTES / 1e6:.0f} MB)"),
         "pct_of_8tbs_nominal": round(100 * value / world / 8000.0, 2),
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                     "traffic": profiled_traffic(w.name)},
+                     "traffic": round(traffic_row * launch_rows) if traffic_row else None,
+                     "traffic_source": "ncu per-row DRAM bytes of a smaller capture x rows per "
+                                       "launch" if traffic_row else None},
+        "dsv3_4096x7168_per_gpu": dsv3,
         "cpu_baseline": cpu,
-        "e2e": {"value": round(e2e_gbs, 3), "unit": "GB/s", "ms_per_step": e2e["ms"],
-                "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"]},
+        "e2e": {"value": round(e2e_gbs, 3), "unit": "GB/s", "ms_per_step": e2e_ms,
+                "h2d_bytes_per_step": e2e["h2d"] * world, "d2h_bytes_per_step": e2e["d2h"] * world,
+                "host_staging_rows_per_gpu": e2e["stage_rows"]},
         "gpu_launches": K,
         "clocks": {"sm_mhz": statistics.median(sm) if sm else None,
                    "sm_max_mhz": clk_all[0]["sm_max_mhz"],
                    "reasons": sorted({r for c in clk_all for r in c["reasons"]}),
-                   "samples": sum(c["samples"] for c in clk_all)},
+                   "samples": sum(c["samples"] for c in clk_all),
+                   "window": "warm-up and timed region (sampler started before the warm-up)"},
     }
     print(json.dumps(line), flush=True)
 
 
 def run_e2e(args, w, rows, dev, g, start, rank, pg):
-    """Same metric through the public host-buffer API: every step copies x and
-    residual from pinned host memory to the GPU, runs the operator and copies
-    residual_out, x_q and x_scale back to pinned host memory, all inside the
-    timed region (the API pipelines row chunks so both PCIe directions and the
-    kernel overlap)."""
+    """Same metric through the public host-buffer API: every step copies the
+    rank's x and residual rows from pinned host memory to the GPU, runs the
+    operator and copies residual_out, x_q and x_scale back to pinned host
+    memory, all inside the timed region (the API pipelines row chunks so both
+    PCIe directions and the kernel overlap). The pinned buffers hold at most
+    ``--e2e-stage-rows`` rows: a larger slab is streamed through them in
+    consecutive API calls, so a step still moves every row of the slab."""
     from flagos_kernelgen_72h_shanghai_2026_b200 import fused_add_rmsnorm_group_quant_host
 
-    x, r, _ = make_inputs(w, device=dev, row_start=start, row_stop=start + rows, seed_offset=rank)
+    stage = min(rows, args.e2e_stage_rows)
+    x, r, _ = make_inputs(w, device=dev, row_start=start, row_stop=start + stage,
+                          seed_offset=rank)
     hx = torch.empty(x.shape, dtype=x.dtype, pin_memory=True)
     hr = torch.empty(r.shape, dtype=r.dtype, pin_memory=True)
     hx.copy_(x)
@@ -336,15 +428,20 @@ def run_e2e(args, w, rows, dev, g, start, rank, pg):
     del x, r
     hro = torch.empty(hx.shape, dtype=hx.dtype, pin_memory=True)
     hq = torch.empty(hx.shape, dtype=w.q_dtype, pin_memory=True)
-    hs = torch.empty(rows, w.groups, dtype=torch.float32, pin_memory=True)
+    hs = torch.empty(stage, w.groups, dtype=torch.float32, pin_memory=True)
     stream = torch.cuda.current_stream(dev)
+    pieces = []
+    for a in range(0, rows, stage):
+        n = min(stage, rows - a)
+        pieces.append(n)
 
     def step():
-        fused_add_rmsnorm_group_quant_host(hx, hr, g, hro, None, hq, hs, w.eps, w.group_size,
-                                           ue8m0=w.ue8m0, device=dev,
-                                           chunk_rows=args.e2e_chunk_rows)
+        for n in pieces:
+            fused_add_rmsnorm_group_quant_host(hx[:n], hr[:n], g, hro[:n], None, hq[:n], hs[:n],
+                                               w.eps, w.group_size, ue8m0=w.ue8m0, device=dev,
+                                               chunk_rows=args.e2e_chunk_rows)
 
-    for _ in range(3):
+    for _ in range(2):
         step()
     torch.cuda.synchronize(dev)
     n = max(3, min(args.e2e_steps, args.steps))
@@ -358,9 +455,10 @@ def run_e2e(args, w, rows, dev, g, start, rank, pg):
         step()
     t1.record(stream)
     torch.cuda.synchronize(dev)
-    h2d = hx.numel() * hx.element_size() + hr.numel() * hr.element_size()
-    d2h = sum(t.numel() * t.element_size() for t in (hro, hq, hs))
-    return {"ms": t0.elapsed_time(t1) / n, "h2d": h2d, "d2h": d2h}
+    per_row_in = w.D * hx.element_size() * 2
+    per_row_out = w.D * (hro.element_size() + hq.element_size()) + w.groups * 4
+    return {"ms": t0.elapsed_time(t1) / n, "h2d": rows * per_row_in, "d2h": rows * per_row_out,
+            "stage_rows": stage}
 
 
 def run_tp(args, w, rank, world, local):
@@ -419,21 +517,108 @@ def run_tp(args, w, rank, world, local):
     dist.destroy_process_group()
 
 
+def run_latency(args, local):
+    """Small-M latency regime (M <= 128, where the reference's launch
+    overhead dominates): host microseconds per eager call (the Python
+    wrapper, argument struct and launch; measured on the host clock over
+    calls issued back to back), device microseconds per call (CUDA events,
+    eager), and device microseconds per call when the calls are replayed from
+    one CUDA graph. Prints its own JSON line; not the default benchmark."""
+    from flagos_kernelgen_72h_shanghai_2026_b200 import fused_add_rmsnorm_group_quant
+    from flagos_kernelgen_72h_shanghai_2026_b200._build import build_lib
+
+    build_lib()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    res = {}
+    for M in (1, 32, 128):
+        w = CONFIGS[2].with_rows(M)
+        x, r, g = make_inputs(w, device=dev)
+        ro, no, q, s = alloc_outputs(w, M, dev)
+
+        def call():
+            fused_add_rmsnorm_group_quant(x, r, g, ro, no, q, s, w.eps, w.group_size)
+
+        for _ in range(50):
+            call()
+        torch.cuda.synchronize(dev)
+        n = 2000
+        t0 = time.perf_counter()
+        for _ in range(n):
+            call()
+        host_us = (time.perf_counter() - t0) / n * 1e6
+        torch.cuda.synchronize(dev)
+        # the same calls with the argument-struct cache emptied before each
+        # one: the full Python-side checks and struct fill every time
+        from flagos_kernelgen_72h_shanghai_2026_b200 import task01
+        t0 = time.perf_counter()
+        for _ in range(n):
+            task01._tls.args = {}
+            call()
+        host_us_nocache = (time.perf_counter() - t0) / n * 1e6
+        torch.cuda.synchronize(dev)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(n):
+            call()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        eager_us = e0.elapsed_time(e1) / n * 1e3
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            call()
+            torch.cuda.synchronize(dev)
+            with torch.cuda.graph(graph, stream=side):
+                for _ in range(100):
+                    call()
+        torch.cuda.synchronize(dev)
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        e0.record()
+        for _ in range(20):
+            graph.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        graph_us = e0.elapsed_time(e1) / 2000 * 1e3
+        res[f"M{M}"] = {"host_us_per_call": round(host_us, 2),
+                        "host_us_per_call_uncached": round(host_us_nocache, 2),
+                        "device_us_per_call_eager": round(eager_us, 2),
+                        "device_us_per_call_graph": round(graph_us, 2)}
+    print(json.dumps({"metric": "small-M latency, us/call (D = 7168, bf16 -> e4m3)",
+                      "mode": "latency", "n_gpus": 1, "higher_is_better": False,
+                      "config": {"workload": "cfg2 shape with M in {1, 32, 128}", "D": 7168},
+                      "us_per_call": res}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20000)
-    ap.add_argument("--warmup", type=int, default=200)
-    ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--config", type=int, default=5, choices=sorted(CONFIGS),
+                    help="workload (default 5: 262144 x 7168 split over the GPUs; the "
+                         "DeepSeek-V3 4096 x 7168 per-GPU figure is reported beside it)")
+    ap.add_argument("--rows", type=int, default=0,
+                    help="override the workload's total rows (small cases for ncu captures)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--mode", default="rows", choices=["rows", "tp"],
+    ap.add_argument("--mode", default="rows", choices=["rows", "tp", "latency"],
                     help="rows: the operator on row shards (default benchmark); tp: the "
-                         "tensor-parallel variant (all-reduce fused with the operator)")
+                         "tensor-parallel variant (all-reduce fused with the operator); "
+                         "latency: small-M host and device cost per call")
     ap.add_argument("--scaling", default=None, choices=["weak", "strong"],
                     help="weak: every GPU runs the full config (default except config 5); "
                          "strong: the config's rows are split over the GPUs (default for config 5)")
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--e2e-chunk-rows", type=int, default=512)
+    ap.add_argument("--e2e-stage-rows", type=int, default=32768,
+                    help="rows of pinned host memory per GPU for the e2e leg")
+    ap.add_argument("--min-warm-s", type=float, default=0.5,
+                    help="extend the warm-up until the GPU has been busy this long")
+    ap.add_argument("--no-dsv3", action="store_true",
+                    help="skip the extra DeepSeek-V3 4096 x 7168 per-GPU figure")
     ap.add_argument("--cpu-budget", type=float, default=12.0,
                     help="seconds of CPU work for the CPU baseline sample")
     ap.add_argument("--ref-budget", type=float, default=90.0,
@@ -449,8 +634,13 @@ def main():
         if world == 1 and args.gpus > 1:
             ap.error("run N > 1 under torchrun (one process per GPU)")
     w = CONFIGS[args.config]
+    if args.rows > 0:
+        w = w.with_rows(args.rows)
     if args.mode == "tp":
         run_tp(args, w, rank, world, local)
+        return
+    if args.mode == "latency":
+        run_latency(args, local)
         return
     if args.impl == "reference":
         run_reference_arm(args, w, rank, world)

@@ -184,6 +184,23 @@ int check_shape(int64_t M, int64_t D, int G) {
   return FARQ_OK;
 }
 
+// Checks of a farq_args_t that need no pointer and no device: struct size,
+// reserved field, shape, group size and dtypes. Shared by farq_launch and
+// farq_launch_host_noalloc (which must reject a call before it queues any
+// copy).
+int validate_args(const farq_args_t* a) {
+  if (!a) return FARQ_ERR_NULL_POINTER;
+  if (a->struct_size != sizeof(farq_args_t) || a->reserved0 != 0) return FARQ_ERR_BAD_ARGS_SIZE;
+  int st = check_shape(a->M, a->D, a->group_size);
+  if (st != FARQ_OK) return st;
+  if (a->x_dtype != FARQ_DTYPE_BF16 && a->x_dtype != FARQ_DTYPE_FP16) return FARQ_ERR_BAD_DTYPE;
+  if (!is_float_out(a->gamma_dtype) || !is_float_out(a->residual_out_dtype))
+    return FARQ_ERR_BAD_DTYPE;
+  if (a->norm_out && !is_float_out(a->norm_out_dtype)) return FARQ_ERR_BAD_DTYPE;
+  if (a->q_dtype != FARQ_DTYPE_INT8 && a->q_dtype != FARQ_DTYPE_E4M3) return FARQ_ERR_BAD_DTYPE;
+  return FARQ_OK;
+}
+
 // Plan for a validated shape on the current device.
 int plan_for(int64_t M, int64_t D, int G, int x_dtype, bool e4m3, const Tune& tune, int* dev,
              KernelSel* ks, Plan* pl) {
@@ -251,17 +268,10 @@ int farq_plan(int64_t M, int64_t D, int32_t group_size, int32_t x_dtype, int32_t
 }
 
 int farq_launch(const farq_args_t* a, void* stream) {
-  if (!a) return FARQ_ERR_NULL_POINTER;
-  if (a->struct_size != sizeof(farq_args_t) || a->reserved0 != 0) return FARQ_ERR_BAD_ARGS_SIZE;
+  int st = validate_args(a);
+  if (st != FARQ_OK) return st;
   const int64_t M = a->M, D = a->D;
   const int G = a->group_size;
-  int st = check_shape(M, D, G);
-  if (st != FARQ_OK) return st;
-  if (a->x_dtype != FARQ_DTYPE_BF16 && a->x_dtype != FARQ_DTYPE_FP16) return FARQ_ERR_BAD_DTYPE;
-  if (!is_float_out(a->gamma_dtype) || !is_float_out(a->residual_out_dtype))
-    return FARQ_ERR_BAD_DTYPE;
-  if (a->norm_out && !is_float_out(a->norm_out_dtype)) return FARQ_ERR_BAD_DTYPE;
-  if (a->q_dtype != FARQ_DTYPE_INT8 && a->q_dtype != FARQ_DTYPE_E4M3) return FARQ_ERR_BAD_DTYPE;
   if (M == 0) return FARQ_OK;
   if (!a->x || !a->residual || !a->gamma || !a->residual_out || !a->x_q || !a->x_scale)
     return FARQ_ERR_NULL_POINTER;

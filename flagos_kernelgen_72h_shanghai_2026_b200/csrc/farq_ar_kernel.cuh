@@ -160,6 +160,10 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_ar_kernel(const ArPara
     // finished with the previous contents of its output buffers.
     // (test-only flag: wait for an epoch no rank signals)
     s_fail = ar_barrier(p, 0, p.force_timeout ? p.epoch + 0x40000000u : p.epoch) ? 0 : 1;
+    // The barrier's acquire is a generic-proxy operation; the peer rows are
+    // read by bulk copies (async proxy), which it orders only after this
+    // proxy fence.
+    asm volatile("fence.proxy.async.global;" ::: "memory");
     for (int s = 0; s < S; ++s) {
       seq[s] = (uint32_t)s;
       if (!s_fail && s < nrows) fill(s, p.row_begin + blockIdx.x + (int64_t)s * G);
@@ -177,6 +181,9 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_ar_kernel(const ArPara
     if (threadIdx.x == 0 && p.status) atomicExch(p.status, (int)FARQ_ERR_DEVICE_TIMEOUT);
     return;
   }
+  // Each team's first thread issues the later refills: it too orders them
+  // (async proxy) after the barrier it observed through __syncthreads.
+  if (tt == 0) asm volatile("fence.proxy.async.global;" ::: "memory");
 
   const float qmax = E4M3 ? 448.0f : 127.0f;
   const int nvec = p.nvec;

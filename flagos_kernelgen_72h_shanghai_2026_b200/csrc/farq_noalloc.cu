@@ -62,28 +62,37 @@ int scratch_address(uint8_t** out) {
   return FARQ_OK;
 }
 
-// Staging bytes one call needs (-1 for a bad shape).
-int64_t noalloc_bytes(int64_t M, int64_t D, int32_t group_size, int32_t x_dtype,
-                                int32_t gamma_dtype, int32_t residual_out_dtype,
-                                int32_t norm_out_dtype, int32_t write_norm) {
-  if (M < 0 || D <= 0 || group_size <= 0 || D % group_size) return -1;
+// Bytes of the array reserved at its start for the status word.
+constexpr size_t kStatusBytes = 256;
+
+// Staging bytes one call needs, for a shape that already passed
+// farq::validate_args (D <= 16384, G in [8, 256]) and M <= the row limit
+// below, so no term can overflow.
+size_t noalloc_bytes(int64_t M, int64_t D, int32_t group_size, int32_t x_dtype,
+                     int32_t gamma_dtype, int32_t residual_out_dtype, int32_t norm_out_dtype,
+                     bool write_norm) {
   const size_t N = (size_t)M * (size_t)D;
-  return (int64_t)(up256(N * elem_size(x_dtype)) * 2 + up256((size_t)D * elem_size(gamma_dtype)) +
-                   up256(N * elem_size(residual_out_dtype)) +
-                   (write_norm ? up256(N * elem_size(norm_out_dtype)) : 0) + up256(N) +
-                   up256((size_t)M * (D / group_size) * 4));
+  return kStatusBytes + up256(N * elem_size(x_dtype)) * 2 +
+         up256((size_t)D * elem_size(gamma_dtype)) + up256(N * elem_size(residual_out_dtype)) +
+         (write_norm ? up256(N * elem_size(norm_out_dtype)) : 0) + up256(N) +
+         up256((size_t)M * (size_t)(D / group_size) * 4);
 }
 
 }  // namespace
 
+namespace farq {
+int validate_args(const farq_args_t* a);  // farq.cu
+}
+
 extern "C" {
 
 int farq_launch_host_noalloc(const farq_args_t* a, void* stream) {
-  if (!a) return FARQ_ERR_NULL_POINTER;
-  if (a->struct_size != sizeof(farq_args_t)) return FARQ_ERR_BAD_ARGS_SIZE;
+  // Every check comes before the first copy is queued, so a rejected call
+  // leaves nothing in flight that still reads or writes the caller's buffers.
+  int st = farq::validate_args(a);
+  if (st != FARQ_OK) return st;
   const int64_t M = a->M, D = a->D;
   const int G = a->group_size;
-  if (M < 0 || D <= 0 || G <= 0 || D % G) return FARQ_ERR_BAD_SHAPE;
   // Host tensors must be contiguous: row strides 0 or the natural ones.
   if ((a->x_row_stride && a->x_row_stride != D) ||
       (a->residual_row_stride && a->residual_row_stride != D) ||
@@ -93,23 +102,25 @@ int farq_launch_host_noalloc(const farq_args_t* a, void* stream) {
       (a->x_scale_row_stride && a->x_scale_row_stride != D / G) ||
       (a->flags & FARQ_FLAG_SCALE_COLUMN_MAJOR))
     return FARQ_ERR_BAD_SHAPE;
-  const int xs = elem_size(a->x_dtype), gs = elem_size(a->gamma_dtype),
-            ros = elem_size(a->residual_out_dtype), nos = elem_size(a->norm_out_dtype);
-  if (!xs || !gs || !ros || (a->norm_out && !nos)) return FARQ_ERR_BAD_DTYPE;
   if (M == 0) return FARQ_OK;
   if (!a->x || !a->residual || !a->gamma || !a->residual_out || !a->x_q || !a->x_scale)
     return FARQ_ERR_NULL_POINTER;
-  const int64_t need = noalloc_bytes(M, D, G, a->x_dtype, a->gamma_dtype,
-                                               a->residual_out_dtype, a->norm_out_dtype,
-                                               a->norm_out != nullptr);
-  if (need < 0) return FARQ_ERR_BAD_SHAPE;
-  if ((size_t)need > kNoAllocScratchBytes) return FARQ_ERR_NOALLOC_TOO_LARGE;
+  // Every row stages at least its D quantised bytes, so more rows than
+  // this can never fit; checking it first keeps the size sum below from
+  // wrapping around for absurd M.
+  if (M > (int64_t)(kNoAllocScratchBytes / (size_t)D)) return FARQ_ERR_NOALLOC_TOO_LARGE;
+  const size_t need = noalloc_bytes(M, D, G, a->x_dtype, a->gamma_dtype, a->residual_out_dtype,
+                                    a->norm_out_dtype, a->norm_out != nullptr);
+  if (need > kNoAllocScratchBytes) return FARQ_ERR_NOALLOC_TOO_LARGE;
 
   uint8_t* base = nullptr;
-  int st = scratch_address(&base);
+  st = scratch_address(&base);
   if (st != FARQ_OK) return st;
+  const int xs = elem_size(a->x_dtype), gs = elem_size(a->gamma_dtype),
+            ros = elem_size(a->residual_out_dtype), nos = elem_size(a->norm_out_dtype);
   const size_t N = (size_t)M * (size_t)D;
-  uint8_t* dx = base;
+  int32_t* dstatus = reinterpret_cast<int32_t*>(base);
+  uint8_t* dx = base + kStatusBytes;
   uint8_t* dr = dx + up256(N * xs);
   uint8_t* dg = dr + up256(N * xs);
   uint8_t* dro = dg + up256((size_t)D * gs);
@@ -118,7 +129,13 @@ int farq_launch_host_noalloc(const farq_args_t* a, void* stream) {
   uint8_t* ds = dq + up256(N);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
 
-  if (cudaMemcpyAsync(dx, a->x, N * xs, cudaMemcpyHostToDevice, s) != cudaSuccess ||
+  // The status word, when given, is a host int here: it is carried to the
+  // device with the inputs and back with the outputs, keeping its contract
+  // (set on a device timeout, never cleared by the library).
+  if ((a->status &&
+       cudaMemcpyAsync(dstatus, a->status, sizeof(int32_t), cudaMemcpyHostToDevice, s) !=
+           cudaSuccess) ||
+      cudaMemcpyAsync(dx, a->x, N * xs, cudaMemcpyHostToDevice, s) != cudaSuccess ||
       cudaMemcpyAsync(dr, a->residual, N * xs, cudaMemcpyHostToDevice, s) != cudaSuccess ||
       cudaMemcpyAsync(dg, a->gamma, (size_t)D * gs, cudaMemcpyHostToDevice, s) != cudaSuccess)
     return FARQ_ERR_CUDA;
@@ -130,8 +147,11 @@ int farq_launch_host_noalloc(const farq_args_t* a, void* stream) {
   d.norm_out = a->norm_out ? dno : nullptr;
   d.x_q = dq;
   d.x_scale = reinterpret_cast<float*>(ds);
+  d.status = a->status ? dstatus : nullptr;
   d.x_row_stride = d.residual_row_stride = d.residual_out_row_stride = 0;
   d.norm_out_row_stride = d.x_q_row_stride = d.x_scale_row_stride = 0;
+  // Everything farq_launch checks beyond validate_args concerns the staged
+  // device pointers, which are 256-byte aligned and contiguous.
   st = farq_launch(&d, stream);
   if (st != FARQ_OK) return st;
   if (cudaMemcpyAsync(a->residual_out, dro, N * ros, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
@@ -139,7 +159,10 @@ int farq_launch_host_noalloc(const farq_args_t* a, void* stream) {
        cudaMemcpyAsync(a->norm_out, dno, N * nos, cudaMemcpyDeviceToHost, s) != cudaSuccess) ||
       cudaMemcpyAsync(a->x_q, dq, N, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
       cudaMemcpyAsync(a->x_scale, ds, (size_t)M * (D / G) * 4, cudaMemcpyDeviceToHost, s) !=
-          cudaSuccess)
+          cudaSuccess ||
+      (a->status &&
+       cudaMemcpyAsync(a->status, dstatus, sizeof(int32_t), cudaMemcpyDeviceToHost, s) !=
+           cudaSuccess))
     return FARQ_ERR_CUDA;
   return FARQ_OK;
 }

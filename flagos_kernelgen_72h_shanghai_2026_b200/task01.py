@@ -26,6 +26,7 @@ when a CUDA call fails. There is no CPU fallback.
 from __future__ import annotations
 
 import ctypes
+import threading
 
 import torch
 
@@ -64,6 +65,35 @@ def _row_stride(name: str, t: torch.Tensor, rows: int, cols: int) -> int:
     return t.stride(0) if rows > 1 else cols
 
 
+# Per-thread cache of filled argument structs keyed by every piece of tensor
+# metadata the Python checks read (device, shape, strides, dtype of each
+# tensor) and the scalar arguments. A hit skips the Python-side checks and
+# the struct fill: only the data pointers change. farq_launch still validates
+# every call (alignment of the new pointers included).
+_tls = threading.local()
+_CACHE_MAX = 64
+
+
+def _meta(t):
+    return (t.device, t.shape, t.stride(), t.dtype)
+
+
+def _launch(a, device):
+    lib = _lib.load()
+    if torch.cuda.current_device() != device.index:
+        with torch.cuda.device(device):
+            st = lib.farq_launch(ctypes.byref(a), torch.cuda.current_stream(device).cuda_stream)
+    else:
+        st = lib.farq_launch(ctypes.byref(a), torch.cuda.current_stream(device).cuda_stream)
+    if st != _lib.OK:
+        msg = f"farq_launch failed: {_lib.strerror(st)} (status {st})"
+        if st in _VALUE_ERRORS:
+            raise ValueError(msg)
+        if st == _lib.ERR_BAD_DTYPE:
+            raise TypeError(msg)
+        raise RuntimeError(msg)
+
+
 def fused_add_rmsnorm_group_quant(
     x: torch.Tensor,
     residual: torch.Tensor,
@@ -86,6 +116,28 @@ def fused_add_rmsnorm_group_quant(
     """residual_out = x + residual; norm = RMSNorm(residual_out) * gamma;
     per-group quantisation of norm into (x_q, x_scale). Asynchronous on the
     current CUDA stream; returns (residual_out, norm_out, x_q, x_scale)."""
+    key = None
+    if (isinstance(x, torch.Tensor) and isinstance(residual, torch.Tensor)
+            and isinstance(gamma, torch.Tensor) and isinstance(residual_out, torch.Tensor)
+            and isinstance(x_q, torch.Tensor) and isinstance(x_scale, torch.Tensor)
+            and (norm_out is None or isinstance(norm_out, torch.Tensor))):
+        key = (_meta(x), _meta(residual), _meta(gamma), _meta(residual_out),
+               None if norm_out is None else _meta(norm_out), _meta(x_q), _meta(x_scale),
+               eps, group_size, ue8m0, _tune_ctas_per_sm, _tune_teams_per_cta, _tune_stages,
+               _tune_vec_per_thread, _status is None, _test_force_timeout)
+        cache = getattr(_tls, "args", None)
+        a = cache.get(key) if cache is not None else None
+        if a is not None:
+            a.x = x.data_ptr()
+            a.residual = residual.data_ptr()
+            a.gamma = gamma.data_ptr()
+            a.residual_out = residual_out.data_ptr()
+            a.norm_out = norm_out.data_ptr() if a.norm_out else None
+            a.x_q = x_q.data_ptr()
+            a.x_scale = x_scale.data_ptr()
+            a.status = _status.data_ptr() if _status is not None else None
+            _launch(a, x.device)
+            return residual_out, norm_out, x_q, x_scale
     if not isinstance(x, torch.Tensor):
         raise TypeError(f"x must be a torch.Tensor, got {type(x).__name__}")
     device = x.device
@@ -175,19 +227,14 @@ def fused_add_rmsnorm_group_quant(
     a.x_q_row_stride = sq
     a.x_scale_row_stride = ss
 
-    lib = _lib.load()
-    if torch.cuda.current_device() != device.index:
-        with torch.cuda.device(device):
-            st = lib.farq_launch(ctypes.byref(a), torch.cuda.current_stream(device).cuda_stream)
-    else:
-        st = lib.farq_launch(ctypes.byref(a), torch.cuda.current_stream(device).cuda_stream)
-    if st != _lib.OK:
-        msg = f"farq_launch failed: {_lib.strerror(st)} (status {st})"
-        if st in _VALUE_ERRORS:
-            raise ValueError(msg)
-        if st == _lib.ERR_BAD_DTYPE:
-            raise TypeError(msg)
-        raise RuntimeError(msg)
+    _launch(a, device)
+    if key is not None:
+        cache = getattr(_tls, "args", None)
+        if cache is None:
+            cache = _tls.args = {}
+        if len(cache) >= _CACHE_MAX:
+            cache.pop(next(iter(cache)))
+        cache[key] = a
     return residual_out, norm_out, x_q, x_scale
 
 

@@ -175,10 +175,14 @@ int farq_plan(int64_t M, int64_t D, int32_t group_size, int32_t x_dtype,
  * library, until the process exits; a call needing more staging (inputs,
  * gamma and outputs of all M rows, each rounded up to 256 bytes — about
  * 1,330 rows at D = 7168, bf16 -> e4m3) returns FARQ_ERR_NOALLOC_TOO_LARGE;
- * split the rows. Tensors must be contiguous with row-major x_scale. The
- * first call on a device looks up the array's device address (make it before
- * any stream capture). All calls share the array: calls that overlap on the
- * GPU race; calls on one stream are ordered.
+ * split the rows. Tensors must be contiguous with row-major x_scale. Every
+ * argument check is made before the first copy is queued, so a rejected call
+ * leaves no copy in flight. `status`, when non-NULL, is a HOST int here: it
+ * is copied to the device with the inputs and back with the outputs (set to
+ * a farq_status if a device wait ran out, never cleared). The first call on
+ * a device looks up the array's device address (make it before any stream
+ * capture). All calls share the array: calls that overlap on the GPU
+ * (several streams or host threads) race; calls on one stream are ordered.
  *
  * No counterpart in the reference, which has no host-buffer path.
  */

@@ -142,7 +142,7 @@ def test_noalloc_entry_validation_before_any_device_call(lib):
     assert f(None, None) == _lib.ERR_NULL_POINTER
     a = _args(struct_size=4)
     assert f(ctypes.byref(a), None) == _lib.ERR_BAD_ARGS_SIZE
-    assert f(ctypes.byref(_args(group_size=100)), None) == _lib.ERR_BAD_SHAPE
+    assert f(ctypes.byref(_args(group_size=100)), None) == _lib.ERR_BAD_GROUP
     assert f(ctypes.byref(_args(x_row_stride=2048)), None) == _lib.ERR_BAD_SHAPE  # host tensors contiguous
     assert f(ctypes.byref(_args()), None) == _lib.ERR_NULL_POINTER
     # 100k rows x 7168 needs far more than the 64 MiB staging array: rejected up front
@@ -150,3 +150,34 @@ def test_noalloc_entry_validation_before_any_device_call(lib):
                 x_q=0x5000, x_scale=0x6000)
     assert f(ctypes.byref(big), None) == _lib.ERR_NOALLOC_TOO_LARGE
     assert f(ctypes.byref(_args(M=0)), None) == _lib.OK
+
+
+_HOST_PTRS = dict(x=0x1000, residual=0x2000, gamma=0x3000, residual_out=0x4000, x_q=0x5000,
+                  x_scale=0x6000)
+
+
+@pytest.mark.parametrize("kw,code", [
+    # every check farq_launch makes on the arguments themselves comes before
+    # the first copy: non-NULL (never dereferenced) host pointers prove that
+    # no copy was queued, since queuing one from these addresses would fail
+    # with a CUDA error instead of the validation code
+    (dict(group_size=48, D=4800), _lib.ERR_BAD_GROUP),
+    (dict(x_dtype=_lib.DTYPE_FP32), _lib.ERR_BAD_DTYPE),
+    (dict(q_dtype=_lib.DTYPE_FP16), _lib.ERR_BAD_DTYPE),
+    (dict(residual_out_dtype=_lib.DTYPE_INT8), _lib.ERR_BAD_DTYPE),
+    (dict(norm_out=0x7000, norm_out_dtype=_lib.DTYPE_E4M3), _lib.ERR_BAD_DTYPE),
+    (dict(reserved0=1), _lib.ERR_BAD_ARGS_SIZE),
+    (dict(D=32768), _lib.ERR_UNSUPPORTED),
+    (dict(M=-3), _lib.ERR_BAD_SHAPE),
+    # M = 2^51 at D = 16384, G = 8 with fp32 residual_out: every staging term
+    # is a multiple of 2^64 bytes, so an unchecked size sum wraps to a few KiB
+    (dict(M=1 << 51, D=16384, group_size=8, residual_out_dtype=_lib.DTYPE_FP32),
+     _lib.ERR_NOALLOC_TOO_LARGE),
+    (dict(M=(64 << 20) // 1024 + 1), _lib.ERR_NOALLOC_TOO_LARGE),
+])
+def test_noalloc_entry_rejects_before_queuing_copies(lib, kw, code):
+    f = lib.farq_launch_host_noalloc
+    f.argtypes = [ctypes.POINTER(_lib.FarqArgs), ctypes.c_void_p]
+    f.restype = ctypes.c_int
+    a = _args(**{**_HOST_PTRS, **kw})
+    assert f(ctypes.byref(a), None) == code

@@ -19,8 +19,21 @@ def test_reference_arm_prints_one_json_line():
     assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["cores"] >= 1
     assert d["e2e"] == {"value": d["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}
-    assert d["config"]["workload"] == "cfg2_dsv3_4096x7168"
-    assert d["config"]["rows_per_step"] >= 16
+    assert d["config"]["workload"] == "cfg5_sharded_262144x7168"
+    assert d["scaling"] == "strong" and d["dtype"] == "fp32"
+    assert d["rows_per_step"] >= 16
+
+
+def test_both_arms_share_one_config():
+    """The repo arm and the reference arm build `config` with the same
+    function, so a driver can pair their lines at every N."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+    from flagos_kernelgen_72h_shanghai_2026_b200.workloads import CONFIGS
+    for n in (1, 2, 8):
+        c = bench.line_config(CONFIGS[5], n, "strong")
+        assert c["M"] == 262144 and c["M_per_gpu"] == 262144 // n
+        assert c["bytes_per_call"] == 262144 * 7168 * 7 + 262144 * 56 * 4 + n * 2 * 7168
 
 
 def test_warmup_below_three_is_refused():
