@@ -1,4 +1,5 @@
-"""In-tree build of libfarq.so (the sm_100a kernels behind the C ABI in include/farq.h).
+"""In-tree build of libfarq.so and libdsa_topk.so (the sm_100a kernels behind
+the C ABIs in include/farq.h and include/dsa_topk.h).
 
 The library is compiled with nvcc directly (no torch headers): it exports only
 plain-C entry points, so the Python host binds it with ctypes. The built file
@@ -20,6 +21,10 @@ SOURCES = [CSRC_DIR / "farq.cu", *sorted(CSRC_DIR.glob("farq_inst_*.cu")),
 HEADERS = [INCLUDE_DIR / "farq.h", CSRC_DIR / "farq_kernel.cuh", CSRC_DIR / "farq_ar_kernel.cuh"]
 LIB_PATH = PKG_DIR / "libfarq.so"
 
+TOPK_SOURCES = [CSRC_DIR / "dsa_topk.cu"]
+TOPK_HEADERS = [INCLUDE_DIR / "dsa_topk.h", CSRC_DIR / "dsa_topk_kernel.cuh"]
+TOPK_LIB_PATH = PKG_DIR / "libdsa_topk.so"
+
 OBJ_DIR = PKG_DIR / "_build"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -34,11 +39,19 @@ def _nvcc() -> str:
     return cand
 
 
-def is_stale() -> bool:
-    if not LIB_PATH.exists():
+def _stale(lib: Path, deps: list[Path]) -> bool:
+    if not lib.exists():
         return True
-    t = LIB_PATH.stat().st_mtime
-    return any(p.stat().st_mtime > t for p in SOURCES + HEADERS)
+    t = lib.stat().st_mtime
+    return any(p.stat().st_mtime > t for p in deps)
+
+
+def is_stale() -> bool:
+    return _stale(LIB_PATH, SOURCES + HEADERS)
+
+
+def is_topk_stale() -> bool:
+    return _stale(TOPK_LIB_PATH, TOPK_SOURCES + TOPK_HEADERS)
 
 
 def _run(cmd: list[str], verbose: bool) -> str:
@@ -51,12 +64,26 @@ def _run(cmd: list[str], verbose: bool) -> str:
 
 
 def build_lib(force: bool = False, verbose: bool = False) -> Path:
-    """Compile libfarq.so for sm_100a if it is missing or older than its sources.
-
-    Each translation unit is compiled to an object in parallel (the kernel
-    instantiations dominate), then linked into one shared library."""
+    """Compile libfarq.so for sm_100a if it is missing or older than its sources."""
     if not force and not is_stale():
         return LIB_PATH
+    return _compile(SOURCES, LIB_PATH, verbose)
+
+
+def build_topk_lib(force: bool = False, verbose: bool = False) -> Path:
+    """Compile libdsa_topk.so for sm_100a if it is missing or older than its sources."""
+    if not force and not is_topk_stale():
+        return TOPK_LIB_PATH
+    return _compile(TOPK_SOURCES, TOPK_LIB_PATH, verbose)
+
+
+def build_all(force: bool = False, verbose: bool = False) -> list[Path]:
+    return [build_lib(force, verbose), build_topk_lib(force, verbose)]
+
+
+def _compile(sources: list[Path], lib_path: Path, verbose: bool) -> Path:
+    """Each translation unit is compiled to an object in parallel (the kernel
+    instantiations dominate), then linked into one shared library."""
     from concurrent.futures import ThreadPoolExecutor
 
     nvcc = _nvcc()
@@ -65,7 +92,7 @@ def build_lib(force: bool = False, verbose: bool = False) -> Path:
     if verbose:
         flags.append("-Xptxas=-v")
     jobs = []
-    for src in SOURCES:
+    for src in sources:
         obj = OBJ_DIR / (src.stem + ".o")
         jobs.append(([nvcc, *flags, "-c", "-o", str(obj), str(src)], obj))
     with ThreadPoolExecutor(max_workers=min(len(jobs), os.cpu_count() or 1)) as ex:
@@ -74,12 +101,12 @@ def build_lib(force: bool = False, verbose: bool = False) -> Path:
         for log in logs:
             if log:
                 print(log)
-    tmp = LIB_PATH.with_suffix(".so.tmp")
+    tmp = lib_path.with_suffix(".so.tmp")
     _run([nvcc, *LINK_FLAGS, "-o", str(tmp), *(str(o) for _, o in jobs)], verbose)
-    os.replace(tmp, LIB_PATH)
-    return LIB_PATH
+    os.replace(tmp, lib_path)
+    return lib_path
 
 
 if __name__ == "__main__":
     import sys
-    print(build_lib(force="--force" in sys.argv, verbose="-v" in sys.argv))
+    print(build_all(force="--force" in sys.argv, verbose="-v" in sys.argv))
