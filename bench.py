@@ -517,6 +517,183 @@ def run_tp(args, w, rank, world, local):
     dist.destroy_process_group()
 
 
+def run_topk(args, rank, world, local):
+    """Task 02, the DSA top-k page-table transform, at its largest competition
+    shape (fp32 scores, 32768 rows x 4096 blocks, K = 128). Metric: algorithmic
+    HBM GB/s (every candidate score read once, ids and pages written, page
+    entries gathered: R * (4 NB + 12 K) + 8 R bytes) and us/call. Rows shard
+    over GPUs (weak scaling: every GPU runs the full shape, no collective).
+    Prints its own JSON line; not the default benchmark."""
+    from flagos_kernelgen_72h_shanghai_2026_b200 import dsa_topk_page_table_transform
+    from flagos_kernelgen_72h_shanghai_2026_b200._build import build_topk_lib
+    from flagos_kernelgen_72h_shanghai_2026_b200.topk_workloads import (
+        TOPK_CONFIGS, make_topk_inputs, topk_bytes_per_call)
+
+    w = TOPK_CONFIGS[args.topk_config]
+    if args.rows > 0:
+        w = w.with_(B=1, H=1, Q=args.rows)
+    if rank != 0 and args.impl == "reference":
+        return
+    if args.impl == "reference":
+        run_topk_reference(args, w, world)
+        return
+    build_topk_lib()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    pg = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+        pg = dist
+    per = topk_bytes_per_call(w)
+    nsets = 1 if per >= 3 * L2_BYTES else min(16, max(2, -(-(3 * L2_BYTES) // per)))
+    s, pt, qp, kv = make_topk_inputs(w.with_(seed=w.seed + rank), device=dev)
+    sets = [(s if i == 0 else s.roll(i, dims=2).contiguous()) for i in range(nsets)]
+    ob = torch.empty(w.B, w.H, w.Q, w.top_k, dtype=torch.int32, device=dev)
+    op = torch.empty_like(ob)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(i):
+        dsa_topk_page_table_transform(sets[i % nsets], pt, qp, kv, ob, op, w.block_size, w.top_k)
+
+    K = args.steps
+    with ClockSampler(smi_index(local)) as clocks:
+        total_ms, warm_run = timed_steps(step, K, args.warmup, stream, dev, pg, args.min_warm_s)
+    clk = clocks.summary()
+
+    # end to end: pinned host scores / page table / positions -> device ->
+    # kernel -> ids and pages back to pinned host memory, every step
+    hs = torch.empty(s.shape, dtype=s.dtype, pin_memory=True)
+    hs.copy_(s)
+    hpt, hqp, hkv = (t.cpu().pin_memory() for t in (pt, qp, kv))
+    hob = torch.empty(ob.shape, dtype=ob.dtype, pin_memory=True)
+    hop = torch.empty_like(hob).pin_memory()
+    ds = torch.empty_like(s)
+    dpt, dqp, dkv = torch.empty_like(pt), torch.empty_like(qp), torch.empty_like(kv)
+
+    def e2e_step():
+        ds.copy_(hs, non_blocking=True)
+        dpt.copy_(hpt, non_blocking=True)
+        dqp.copy_(hqp, non_blocking=True)
+        dkv.copy_(hkv, non_blocking=True)
+        dsa_topk_page_table_transform(ds, dpt, dqp, dkv, ob, op, w.block_size, w.top_k)
+        hob.copy_(ob, non_blocking=True)
+        hop.copy_(op, non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize(dev)
+    n_e2e = max(3, min(args.e2e_steps, K))
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    if pg:
+        pg.barrier()
+    e0.record(stream)
+    for _ in range(n_e2e):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = e0.elapsed_time(e1) / n_e2e
+    h2d = sum(t.numel() * t.element_size() for t in (hs, hpt, hqp, hkv))
+    d2h = sum(t.numel() * t.element_size() for t in (hob, hop))
+
+    times = torch.tensor([total_ms, e2e_ms], dtype=torch.float64, device=dev)
+    if pg:
+        pg.all_reduce(times, op=pg.ReduceOp.MAX)
+        clk_all = [None] * world
+        pg.all_gather_object(clk_all, clk)
+    else:
+        clk_all = [clk]
+    total_ms, e2e_ms = float(times[0]), float(times[1])
+    ms = total_ms / K
+    value = per * world / (ms * 1e-3) / 1e9
+    peak, peak_kind = load_peak()
+    achieved = per / (ms * 1e-3) / 1e9
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        gbs, dt, rows, cores = topk_cpu_sample(w, budget_s=args.cpu_budget)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+               "sample": f"{rows} of {w.rows} rows of {w.name} per call, numpy restatement of "
+                         f"the reference (oracle/dsa_topk_oracle.py, single thread)"}
+    if pg:
+        pg.destroy_process_group()
+    if rank != 0:
+        return
+    sm = [c["sm_mhz"] for c in clk_all if c["sm_mhz"]]
+    print(json.dumps({
+        "metric": TOPK_METRIC, "mode": "topk", "value": round(value, 2), "unit": "GB/s",
+        "n_gpus": world, "steps": K, "warmup": warm_run, "ms_per_step": ms,
+        "us_per_call": ms * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32", "data": "synthetic (seeded torch.randn scores)",
+        "config": topk_line_config(w, world),
+        "l2": f"inputs larger than L2: {nsets} rotating score set(s) of {per / 1e6:.0f} MB",
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
+                     "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "traffic": None},
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(per * world / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
+                "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d * world,
+                "d2h_bytes_per_step": d2h * world},
+        "gpu_launches": K,
+        "clocks": {"sm_mhz": statistics.median(sm) if sm else None,
+                   "sm_max_mhz": clk_all[0]["sm_max_mhz"],
+                   "reasons": sorted({r for c in clk_all for r in c["reasons"]}),
+                   "samples": sum(c["samples"] for c in clk_all)},
+    }), flush=True)
+
+
+TOPK_METRIC = "DSA top-k page-table transform: algorithmic HBM GB/s and us/call"
+
+
+def topk_line_config(w, world):
+    from flagos_kernelgen_72h_shanghai_2026_b200.topk_workloads import topk_bytes_per_call
+    return {"workload": w.name, "B": w.B, "H": w.H, "Q": w.Q, "NB": w.NB, "top_k": w.top_k,
+            "block_size": w.block_size, "scores_dtype": str(w.dtype).replace("torch.", ""),
+            "bytes_per_call": topk_bytes_per_call(w) * world,
+            "parallelism": f"full shape on each of {world} GPU(s), no collective"}
+
+
+def topk_cpu_sample(w, budget_s: float):
+    """Time the numpy restatement of the reference (the oracle) on a bounded
+    row sample of ``w``. Returns (GB/s, seconds per call, rows, cores)."""
+    from oracle.dsa_topk_oracle import dsa_topk_page_table_transform_ref
+    from flagos_kernelgen_72h_shanghai_2026_b200.topk_workloads import (
+        make_topk_inputs, topk_bytes_per_call)
+    probe = w.with_(B=1, H=1, Q=min(256, w.rows))
+    s, pt, qp, kv = make_topk_inputs(probe)
+    t0 = time.perf_counter()
+    dsa_topk_page_table_transform_ref(s, pt, qp, kv, w.block_size, w.top_k)
+    per_row = (time.perf_counter() - t0) / probe.rows
+    rows = max(64, min(w.rows, int(budget_s / 4 / max(per_row, 1e-9))))
+    sample = w.with_(B=1, H=1, Q=rows)
+    s, pt, qp, kv = make_topk_inputs(sample)
+    dsa_topk_page_table_transform_ref(s, pt, qp, kv, w.block_size, w.top_k)
+    t0 = time.perf_counter()
+    for _ in range(3):
+        dsa_topk_page_table_transform_ref(s, pt, qp, kv, w.block_size, w.top_k)
+    dt = (time.perf_counter() - t0) / 3
+    return topk_bytes_per_call(sample) / dt / 1e9, dt, rows, 1
+
+
+def run_topk_reference(args, w, world):
+    """Reference arm of --mode topk: the reference is Triton-only (no CPU code
+    of its own), so its CPU stand-in is the numpy restatement, timed on a
+    bounded row sample, rank 0 only."""
+    gbs, dt, rows, cores = topk_cpu_sample(w, budget_s=args.ref_budget / 3)
+    sample = (f"{rows} of {w.rows} rows of {w.name} per step, numpy restatement of the "
+              f"reference (oracle/dsa_topk_oracle.py, single thread)")
+    print(json.dumps({
+        "metric": TOPK_METRIC, "mode": "topk", "value": round(gbs, 3), "unit": "GB/s",
+        "impl": "reference", "n_gpus": world, "steps": 3, "warmup": 1,
+        "ms_per_step": dt * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp32", "data": "synthetic", "config": topk_line_config(w, world),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
 def run_latency(args, local):
     """Small-M latency regime (M <= 128, where the reference's launch
     overhead dominates): host microseconds per eager call (the Python
@@ -604,10 +781,13 @@ def main():
     ap.add_argument("--rows", type=int, default=0,
                     help="override the workload's total rows (small cases for ncu captures)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--mode", default="rows", choices=["rows", "tp", "latency"],
+    ap.add_argument("--mode", default="rows", choices=["rows", "tp", "latency", "topk"],
                     help="rows: the operator on row shards (default benchmark); tp: the "
                          "tensor-parallel variant (all-reduce fused with the operator); "
-                         "latency: small-M host and device cost per call")
+                         "latency: small-M host and device cost per call; topk: the DSA "
+                         "top-k page-table transform (Task 02)")
+    ap.add_argument("--topk-config", default="t2_nb4096_k128_2x32x512",
+                    help="Task 02 workload of --mode topk (topk_workloads.TOPK_CONFIGS)")
     ap.add_argument("--scaling", default=None, choices=["weak", "strong"],
                     help="weak: every GPU runs the full config (default except config 5); "
                          "strong: the config's rows are split over the GPUs (default for config 5)")
@@ -641,6 +821,9 @@ def main():
         return
     if args.mode == "latency":
         run_latency(args, local)
+        return
+    if args.mode == "topk":
+        run_topk(args, rank, world, local)
         return
     if args.impl == "reference":
         run_reference_arm(args, w, rank, world)

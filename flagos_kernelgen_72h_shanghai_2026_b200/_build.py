@@ -93,8 +93,12 @@ def _compile(sources: list[Path], lib_path: Path, verbose: bool) -> Path:
         flags.append("-Xptxas=-v")
     jobs = []
     for src in sources:
-        obj = OBJ_DIR / (src.stem + ".o")
-        jobs.append(([nvcc, *flags, "-c", "-o", str(obj), str(src)], obj))
+        # the tensor-parallel tables are compiled once per WMAX (1, 2, 4, 8)
+        variants = ([(f"_w{w}", [f"-DFARQ_AR_WMAX={w}"]) for w in (1, 2, 4, 8)]
+                    if src.name.startswith("farq_ar_inst_") else [("", [])])
+        for suffix, defs in variants:
+            obj = OBJ_DIR / (src.stem + suffix + ".o")
+            jobs.append(([nvcc, *flags, *defs, "-c", "-o", str(obj), str(src)], obj))
     with ThreadPoolExecutor(max_workers=min(len(jobs), os.cpu_count() or 1)) as ex:
         logs = list(ex.map(lambda j: _run(j[0], verbose), jobs))
     if verbose:

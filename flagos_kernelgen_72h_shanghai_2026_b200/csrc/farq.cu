@@ -23,8 +23,8 @@ std::atomic<int> g_sm_count[kMaxDevices];
 std::atomic<int> g_smem_optin[kMaxDevices];
 std::atomic<int> g_smem_set[kMaxDevices][kSlots];  // largest dynamic smem granted
 std::atomic<int> g_regs[kMaxDevices][kSlots];      // registers per thread (0 = unknown)
-std::atomic<int> g_ar_smem_set[kMaxDevices][kSlots];  // same, tensor-parallel kernels
-std::atomic<int> g_ar_regs[kMaxDevices][kSlots];
+std::atomic<int> g_ar_smem_set[kMaxDevices][kSlots * 4];  // same, tensor-parallel kernels
+std::atomic<int> g_ar_regs[kMaxDevices][kSlots * 4];      // (x4: WMAX 1, 2, 4, 8)
 
 int ilog2(int v) {
   int l = 0;
@@ -397,13 +397,18 @@ int farq_ar_launch(const farq_ar_args_t* a, void* stream) {
   st = pick_k(D / 8, 0, false, &K, &T);
   if (st != FARQ_OK) return st;
   const int gl = ilog2(G / 8);
-  ArKernelFn fn;
   const bool e4m3 = a->q_dtype == FARQ_DTYPE_E4M3;
-  if (a->x_dtype == FARQ_DTYPE_BF16)
-    fn = e4m3 ? ar_kernel_bf16_e4m3(K, gl) : ar_kernel_bf16_int8(K, gl);
-  else
-    fn = e4m3 ? ar_kernel_fp16_e4m3(K, gl) : ar_kernel_fp16_int8(K, gl);
-  const int slot = (((a->x_dtype == FARQ_DTYPE_BF16 ? 0 : 1) * 2 + (e4m3 ? 1 : 0)) * kMaxK + (K - 1)) * 6 + gl;
+  // The kernel compiled for the smallest WMAX in {1, 2, 4, 8} that holds W.
+  const int wi = W <= 1 ? 0 : W <= 2 ? 1 : W <= 4 ? 2 : 3;
+  using TableFn = ArKernelFn (*)(int, int);
+  static const TableFn tables[2][2][4] = {
+      {{ar_kernel_bf16_int8_w1, ar_kernel_bf16_int8_w2, ar_kernel_bf16_int8_w4, ar_kernel_bf16_int8_w8},
+       {ar_kernel_bf16_e4m3_w1, ar_kernel_bf16_e4m3_w2, ar_kernel_bf16_e4m3_w4, ar_kernel_bf16_e4m3_w8}},
+      {{ar_kernel_fp16_int8_w1, ar_kernel_fp16_int8_w2, ar_kernel_fp16_int8_w4, ar_kernel_fp16_int8_w8},
+       {ar_kernel_fp16_e4m3_w1, ar_kernel_fp16_e4m3_w2, ar_kernel_fp16_e4m3_w4, ar_kernel_fp16_e4m3_w8}}};
+  const int ti = a->x_dtype == FARQ_DTYPE_BF16 ? 0 : 1;
+  ArKernelFn fn = tables[ti][e4m3 ? 1 : 0][wi](K, gl);
+  const int slot = ((((ti * 2 + (e4m3 ? 1 : 0)) * kMaxK + (K - 1)) * 6 + gl) * 4) + wi;
   int regs = g_ar_regs[dev][slot].load(std::memory_order_relaxed);
   if (regs <= 0) {
     cudaFuncAttributes fa;

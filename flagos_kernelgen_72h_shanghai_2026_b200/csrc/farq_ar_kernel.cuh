@@ -112,7 +112,10 @@ __device__ __forceinline__ bool ar_barrier(const ArParams& p, int phase, uint32_
   return true;
 }
 
-template <typename Tin, int K, int GL, bool E4M3>
+// WMAX (1, 2, 4 or 8) bounds the world size W at compile time: the loops
+// over ranks unroll to WMAX with a guard for W < WMAX, so a world of one or
+// two ranks carries no code for eight.
+template <typename Tin, int K, int GL, bool E4M3, int WMAX>
 __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_ar_kernel(const ArParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const ArLayout L = ar_layout(p.D, p.row_bytes, p.world, p.teams, p.stages);
@@ -147,7 +150,7 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_ar_kernel(const ArPara
     const uint32_t dst = smem_u32(ring + (size_t)slot * slot_bytes);
     mbar_arrive_expect_tx(bar, slot_bytes);
 #pragma unroll
-    for (int k = 0; k < kMaxWorld; ++k)  // constant indices keep the peer pointers out of memory
+    for (int k = 0; k < WMAX; ++k)  // constant indices keep the peer pointers out of memory
       if (k < W) bulk_load(dst + (uint32_t)k * rb, p.part[k] + row * rb, rb, bar, pol);
     bulk_load(dst + (uint32_t)W * rb, p.res + row * rb, rb, bar, pol);
   };
@@ -219,10 +222,13 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_ar_kernel(const ArPara
       if (v < nvec) {
         float a[8], b[8];
         Unpack<Tin>::run(reinterpret_cast<const uint4*>(slot)[v], a);
-        for (int rk = 1; rk < W; ++rk) {
-          Unpack<Tin>::run(reinterpret_cast<const uint4*>(slot + (size_t)rk * rb)[v], b);
 #pragma unroll
-          for (int e = 0; e < 8; ++e) a[e] += b[e];
+        for (int rk = 1; rk < WMAX; ++rk) {
+          if (rk < W) {
+            Unpack<Tin>::run(reinterpret_cast<const uint4*>(slot + (size_t)rk * rb)[v], b);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) a[e] += b[e];
+          }
         }
         const uint4 xr = make_uint4(pack2(a[0], a[1], xdt), pack2(a[2], a[3], xdt),
                                     pack2(a[4], a[5], xdt), pack2(a[6], a[7], xdt));
@@ -241,7 +247,7 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_ar_kernel(const ArPara
           m = fmaxf(m, fabsf(w[k][e]));
         }
 #pragma unroll
-        for (int rk = 0; rk < kMaxWorld; ++rk)
+        for (int rk = 0; rk < WMAX; ++rk)
           if (rk < W) store8(p.rout[rk] + row * rb, v, a, xdt);
       } else {
 #pragma unroll
@@ -282,7 +288,7 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_ar_kernel(const ArPara
         for (int e = 0; e < 8; ++e) nrm[e] = w[k][e] * inv_rms;
         if (p.nout[0]) {
 #pragma unroll
-          for (int rk = 0; rk < kMaxWorld; ++rk)
+          for (int rk = 0; rk < WMAX; ++rk)
             if (rk < W)
               store8(p.nout[rk] + row * (int64_t)p.D * (p.nout_dtype == FARQ_DTYPE_FP32 ? 4 : 2),
                      v, nrm, p.nout_dtype);
@@ -298,7 +304,7 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_ar_kernel(const ArPara
                (i8(nrm[7] * isc) << 24);
         }
 #pragma unroll
-        for (int rk = 0; rk < kMaxWorld; ++rk) {
+        for (int rk = 0; rk < WMAX; ++rk) {
           if (rk < W) {
             st_cs_v2(p.q[rk] + row * (int64_t)p.D + 8 * (int64_t)v, lo, hi);
             if ((lane & (GL - 1)) == 0) st_cs_f32(p.scale[rk] + row * groups + v / GL, sc);
@@ -335,27 +341,38 @@ __global__ void __launch_bounds__(kMaxCtaThreads, 1) farq_ar_kernel(const ArPara
 }
 
 using ArKernelFn = void (*)(const ArParams);
-ArKernelFn ar_kernel_bf16_int8(int K, int gl_log2);
-ArKernelFn ar_kernel_bf16_e4m3(int K, int gl_log2);
-ArKernelFn ar_kernel_fp16_int8(int K, int gl_log2);
-ArKernelFn ar_kernel_fp16_e4m3(int K, int gl_log2);
+// Kernel tables by (K, log2 GL), one per input/output type and WMAX; the
+// farq_ar_inst_*.cu sources are compiled once per WMAX (-DFARQ_AR_WMAX=w).
+#define FARQ_AR_DECLARE(NAME)            \
+  ArKernelFn NAME##_w1(int K, int gl_log2); \
+  ArKernelFn NAME##_w2(int K, int gl_log2); \
+  ArKernelFn NAME##_w4(int K, int gl_log2); \
+  ArKernelFn NAME##_w8(int K, int gl_log2);
+FARQ_AR_DECLARE(ar_kernel_bf16_int8)
+FARQ_AR_DECLARE(ar_kernel_bf16_e4m3)
+FARQ_AR_DECLARE(ar_kernel_fp16_int8)
+FARQ_AR_DECLARE(ar_kernel_fp16_e4m3)
+#undef FARQ_AR_DECLARE
 
 }  // namespace farq
 
+#define FARQ_AR_CAT2(a, b) a##b
+#define FARQ_AR_CAT(a, b) FARQ_AR_CAT2(a, b)
 #define FARQ_AR_KERNEL_TABLE(NAME, TIN, E4M3)                                           \
   namespace farq {                                                                      \
   template <int K>                                                                      \
   static ArKernelFn NAME##_k(int gl_log2) {                                             \
+    constexpr int W = FARQ_AR_WMAX;                                                     \
     switch (gl_log2) {                                                                  \
-      case 0: return farq_ar_kernel<TIN, K, 1, E4M3>;                                   \
-      case 1: return farq_ar_kernel<TIN, K, 2, E4M3>;                                   \
-      case 2: return farq_ar_kernel<TIN, K, 4, E4M3>;                                   \
-      case 3: return farq_ar_kernel<TIN, K, 8, E4M3>;                                   \
-      case 4: return farq_ar_kernel<TIN, K, 16, E4M3>;                                  \
-      default: return farq_ar_kernel<TIN, K, 32, E4M3>;                                 \
+      case 0: return farq_ar_kernel<TIN, K, 1, E4M3, W>;                                \
+      case 1: return farq_ar_kernel<TIN, K, 2, E4M3, W>;                                \
+      case 2: return farq_ar_kernel<TIN, K, 4, E4M3, W>;                                \
+      case 3: return farq_ar_kernel<TIN, K, 8, E4M3, W>;                                \
+      case 4: return farq_ar_kernel<TIN, K, 16, E4M3, W>;                               \
+      default: return farq_ar_kernel<TIN, K, 32, E4M3, W>;                              \
     }                                                                                   \
   }                                                                                     \
-  ArKernelFn NAME(int K, int gl_log2) {                                                 \
+  ArKernelFn FARQ_AR_CAT(NAME##_w, FARQ_AR_WMAX)(int K, int gl_log2) {                  \
     switch (K) {                                                                        \
       case 1: return NAME##_k<1>(gl_log2);                                              \
       case 2: return NAME##_k<2>(gl_log2);                                              \
