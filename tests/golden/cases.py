@@ -42,7 +42,20 @@ CASES = {
         "_nvidia_parallel_row_group_streaming_kernel"),
     "full_row_1x4096_g128": (
         Workload("g7", 1, 4096, q_dtype=torch.int8, seed=6), (), "_preweighted_full_row_kernel"),
+    # the DeepSeek-V3 benchmark shape (4096 x 7168, residual std 2) in int8
+    "segmented_4096x7168_dsv3_rows": (
+        Workload("g10", 4096, 7168, q_dtype=torch.int8, res_std=2.0, seed=9), (),
+        "_preweighted_segmented_streaming_kernel"),
 }
+
+# Cases whose fixture keeps every n-th row of q and x_scale only (the whole
+# call is run; the stored rows keep the fixture small).
+ROW_STEP = {"segmented_4096x7168_dsv3_rows": 32}
+
+
+def stored_rows(name: str, t: torch.Tensor) -> torch.Tensor:
+    """The rows of a full [M, ...] output that the case's fixture stores."""
+    return t[::ROW_STEP.get(name, 1)]
 
 
 def case_inputs(name: str):

@@ -29,7 +29,7 @@ sys.path.insert(0, str(HERE))
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-from cases import CASES, case_inputs, input_digest  # noqa: E402
+from cases import CASES, case_inputs, input_digest, stored_rows  # noqa: E402
 
 
 def load_reference(path: str):
@@ -53,7 +53,8 @@ def main(ref_path: str, only: list[str]) -> None:
         s = torch.empty(M, D // G, dtype=torch.float32)
         t0 = time.time()
         ref.fused_add_rmsnorm_group_quant(x, r, g, ro, no, q, s, w.eps, G)
-        np.savez_compressed(HERE / f"{name}.npz", q=q.numpy(), scale=s.numpy(),
+        np.savez_compressed(HERE / f"{name}.npz", q=stored_rows(name, q).numpy(),
+                            scale=stored_rows(name, s).numpy(),
                             digest=np.array(input_digest(x, r, g)),
                             kernel=np.array(CASES[name][2]))
         print(f"{name}: {time.time() - t0:.1f}s")
