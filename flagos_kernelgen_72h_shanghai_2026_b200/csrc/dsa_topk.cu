@@ -25,26 +25,38 @@ std::atomic<int> g_occ[kMaxDevices][kSlots];        // resident CTAs per SM (0 =
 std::atomic<int> g_occ_smem[kMaxDevices][kSlots];   // dynamic smem the occupancy was taken at
 std::atomic<int> g_smem_set[kMaxDevices][kSlots];   // dynamic smem granted to the kernel
 
-template <typename T>
+// Instantiated shapes: 128 threads with J = 1..8 (NB <= 4096); 256 and 512
+// threads with J = 5..8 (4096 < NB <= 16384).
+template <typename S, int NT>
 KernelFn pick_j(int J) {
   switch (J) {
-    case 1: return dsa_topk_kernel<T, 1>;
-    case 2: return dsa_topk_kernel<T, 2>;
-    case 3: return dsa_topk_kernel<T, 3>;
-    case 4: return dsa_topk_kernel<T, 4>;
-    case 5: return dsa_topk_kernel<T, 5>;
-    case 6: return dsa_topk_kernel<T, 6>;
-    case 7: return dsa_topk_kernel<T, 7>;
-    case 8: return dsa_topk_kernel<T, 8>;
+    case 1: return NT == 128 ? dsa_topk_kernel<S, 1, 128> : nullptr;
+    case 2: return NT == 128 ? dsa_topk_kernel<S, 2, 128> : nullptr;
+    case 3: return NT == 128 ? dsa_topk_kernel<S, 3, 128> : nullptr;
+    case 4: return NT == 128 ? dsa_topk_kernel<S, 4, 128> : nullptr;
+    case 5: return dsa_topk_kernel<S, 5, NT>;
+    case 6: return dsa_topk_kernel<S, 6, NT>;
+    case 7: return dsa_topk_kernel<S, 7, NT>;
+    case 8: return dsa_topk_kernel<S, 8, NT>;
     default: return nullptr;
   }
 }
 
-KernelFn topk_kernel(int scores_dtype, int J) {
+template <typename S>
+KernelFn pick_t(int J, int T) {
+  switch (T) {
+    case 128: return pick_j<S, 128>(J);
+    case 256: return pick_j<S, 256>(J);
+    case 512: return pick_j<S, 512>(J);
+    default: return nullptr;
+  }
+}
+
+KernelFn topk_kernel(int scores_dtype, int J, int T) {
   switch (scores_dtype) {
-    case DSA_DTYPE_FP32: return pick_j<float>(J);
-    case DSA_DTYPE_BF16: return pick_j<__nv_bfloat16>(J);
-    case DSA_DTYPE_FP16: return pick_j<__half>(J);
+    case DSA_DTYPE_FP32: return pick_t<float>(J, T);
+    case DSA_DTYPE_BF16: return pick_t<__nv_bfloat16>(J, T);
+    case DSA_DTYPE_FP16: return pick_t<__half>(J, T);
     default: return nullptr;
   }
 }
@@ -58,21 +70,21 @@ int score_size(int dt) {
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 // CTA width and vectors per thread for a row of NB scores (nvec = NB / 4
-// four-score vectors, each thread holds J of them). Narrow rows use one
-// vector per thread and 128 or 256 threads (several CTAs share an SM);
-// wider rows keep 256 threads up to 4096 scores (4 vectors each), then 512.
+// four-score vectors, each thread holds J <= 8 of them, i.e. at most 32
+// keys in registers): 128 threads up to NB = 4096, then 256 and 512.
 void pick_shape(int64_t NB, int* T, int* J) {
   const int64_t nvec = NB / 4;
-  if (nvec <= 128) {
-    *T = 128;
-    *J = 1;
-  } else if (nvec <= 256 * 4) {
-    *T = 256;
-    *J = (int)((nvec + 255) / 256);
-  } else {
-    *T = 512;
-    *J = (int)((nvec + 511) / 512);
-  }
+  *T = nvec <= 128 * 8 ? 128 : nvec <= 256 * 8 ? 256 : 512;
+  *J = (int)((nvec + *T - 1) / *T);
+}
+
+// Threads per lower-bound group: the largest power of two g <= 32 that
+// still leaves T / g >= K groups (0 when K > T: no bound).
+int pick_group(int T, int K) {
+  if (K > T) return 0;
+  int g = 1;
+  while (g < 32 && T / (2 * g) >= K) g *= 2;
+  return g;
 }
 
 int validate(const dsa_topk_args_t* a) {
@@ -134,7 +146,7 @@ int dsa_topk_launch(const dsa_topk_args_t* a, void* stream) {
 
   int T, J;
   pick_shape(a->NB, &T, &J);
-  KernelFn fn = topk_kernel(a->scores_dtype, J);
+  KernelFn fn = topk_kernel(a->scores_dtype, J, T);
   if (!fn) return DSA_ERR_UNSUPPORTED;
   const int slot = (a->scores_dtype * kMaxJ + (J - 1)) * 3 + (T == 128 ? 0 : T == 256 ? 1 : 2);
 
@@ -147,7 +159,9 @@ int dsa_topk_launch(const dsa_topk_args_t* a, void* stream) {
       return DSA_ERR_CUDA;
     g_sm_count[dev].store(sms, std::memory_order_relaxed);
   }
-  const int smem = (int)smem_layout(a->top_k).total;
+  const int cap = candidate_cap(a->top_k);
+  const int vec_bytes = score_size(a->scores_dtype) * 4;
+  const int smem = (int)smem_layout(T, J, vec_bytes, a->top_k, cap).total;
   if (smem > g_smem_set[dev][slot].load(std::memory_order_relaxed)) {
     if (cudaFuncSetAttribute(reinterpret_cast<const void*>(fn),
                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
@@ -181,6 +195,8 @@ int dsa_topk_launch(const dsa_topk_args_t* a, void* stream) {
   p.index_bytes = ib;
   p.page_bytes = pb;
   p.blocks_bytes = bb;
+  p.cap = cap;
+  p.group = pick_group(T, a->top_k);
 
   // Programmatic stream serialisation: this launch may start while the
   // previous kernel in the stream drains; the kernel waits for it

@@ -8,25 +8,37 @@
 //   order ................... :489-505  ordered fp32 key (-0 -> +0), then block id ascending
 //   outputs ................. :170-175  ids (-1 when missing), pages = page_table[b*NB + id]
 //
-// Execution model: one CTA of T threads per row at a time (persistent grid,
-// rows blockIdx.x, blockIdx.x + grid, ...). Thread t owns the 4-element
-// vectors v = j*T + t, j < J, of a row, i.e. block ids 4v..4v+3; it loads
-// them (only those inside the row's causal prefix) one row ahead into
-// registers, so the next row's HBM reads overlap this row's selection.
+// Execution model: a persistent grid of CTAs of T threads (128 for NB <=
+// 4096); a CTA takes rows blockIdx.x, blockIdx.x + grid, ... one at a time.
+// Thread t owns the four-score vectors v = j*T + t (j < J) of a row, i.e.
+// block ids 4v..4v+3. The next row's vectors are copied global -> shared by
+// cp.async while the current row is processed (each thread copies and later
+// reads only its own vectors, so no CTA barrier guards the staging buffer).
 //
-// Selection is exact: scores become order-preserving 32-bit keys (0 = not
-// selectable), and the K-th largest key is found by a radix select over the
-// keys held in registers — digit 1 = bits 31..20 (4096-bin shared-memory
-// histogram), then, only for keys in the K-th key's bin, bits 19..10 and
-// bits 9..0 (1024 bins each). A pass stops early once the K-th key's bin can
-// be taken whole. If the K-th key itself occurs several times, the equal
-// keys are taken in block-id order by a block-wide scan (the reference's id
-// tie-break). The `need` = min(K, selectable) winners are then ranked by
-// their 64-bit (key, ~id) codes, and ids and page-table entries are written
-// with coalesced stores.
+// Per row, exactly:
+//  1. keys: every score becomes an order-preserving 32-bit key, 0 for a block
+//     that is not selectable. Per-thread max and count of selectable keys.
+//  2. lower bound: threads are grouped so that there are at least K groups;
+//     every group max is a distinct key, so at least K keys are >= the
+//     smallest group max (t0). One block reduction gives the selectable
+//     count, the row max `hi` and t0.
+//  3. compaction: the keys >= t0 (about 470 of 4096 at K = 128 for Gaussian
+//     scores) are appended to a shared candidate list as 64-bit codes
+//     (key << 32 | ~id), one shared atomic per warp. Codes are unique, so
+//     their order is the exact output order. If more than `cap` keys pass
+//     (heavy ties, K > T), a radix refinement over the register keys raises
+//     the bound first (512-bin digits of key - lo, narrowing by 9 bits per
+//     level); when it reaches a single key value that still has too many
+//     copies, the copies are taken in block-id order by block scans.
+//  4. exact top-K of the candidates: a 512-bin histogram of (key - lo) over
+//     the adaptive range [lo, hi] locates the bin of the K-th code; the
+//     candidates in it and above are scattered into bin segments (descending
+//     bins), and each is ranked inside its own segment (typically 1-3 codes)
+//     by comparing codes. Output slot = segment start + rank.
+//  5. outputs: ids, and pages gathered from page_table, -1 beyond the
+//     selectable count; coalesced stores.
 //
-// No scratch memory: all intermediate state is in registers and shared
-// memory. No device-side waits.
+// No scratch memory in global memory; no device-side waits.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -39,9 +51,10 @@
 namespace dsa {
 
 constexpr int kMaxThreads = 512;
-constexpr int kBins1 = 4096;   // digit 1: key bits 31..20
-constexpr int kBins2 = 1024;   // digits 2 and 3: key bits 19..10, 9..0
+constexpr int kBins = 512;      // histogram digits of 9 bits
+constexpr int kBinBits = 9;
 constexpr int kMaxTopK = 2048;
+constexpr int kMinCap = 1024;   // candidate list capacity (at least K)
 constexpr int64_t kMaxBlocks = 16384;
 
 struct Params {
@@ -60,20 +73,27 @@ struct Params {
   int32_t index_bytes;   // q_pos / kv_lens element size (4 or 8)
   int32_t page_bytes;    // page_table / out_pages element size (4 or 8)
   int32_t blocks_bytes;  // out_blocks element size (4 or 8)
+  int32_t cap;           // candidate list capacity (>= K)
+  int32_t group;         // threads per lower-bound group (power of two <= 32), 0 = no bound
 };
 
 // Shared-memory carve-up (dynamic part), identical on host and device.
 struct Smem {
-  size_t hist, list, outid, total;
+  size_t stage, cand, ord, hist, F, outid, total;
 };
-__host__ __device__ inline Smem smem_layout(int K) {
+__host__ __device__ inline size_t align16(size_t v) { return (v + 15) / 16 * 16; }
+__host__ __device__ inline Smem smem_layout(int T, int J, int vec_bytes, int K, int cap) {
   Smem L;
-  L.hist = 0;
-  L.list = L.hist + kBins1 * sizeof(uint32_t);
-  L.outid = L.list + (size_t)K * sizeof(uint64_t);
-  L.total = L.outid + ((size_t)K * sizeof(int32_t) + 15) / 16 * 16;
+  L.stage = 0;
+  L.cand = align16((size_t)T * J * vec_bytes);
+  L.ord = L.cand + (size_t)cap * sizeof(uint64_t);
+  L.hist = L.ord + (size_t)cap * sizeof(uint64_t);
+  L.F = L.hist + align16((kBins + 1) * sizeof(uint32_t));
+  L.outid = L.F + align16((kBins + 1) * sizeof(uint32_t));
+  L.total = L.outid + align16((size_t)K * sizeof(int32_t));
   return L;
 }
+__host__ __device__ inline int candidate_cap(int K) { return K > kMinCap ? K : kMinCap; }
 
 // ------------------------------------------------------------------ loads
 template <typename T>
@@ -81,13 +101,7 @@ struct Vec4;  // raw storage of 4 scores
 template <>
 struct Vec4<float> {
   using raw = uint4;
-  __device__ __forceinline__ static raw load(const float* p) {
-    raw v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
-  }
+  static constexpr int kBytes = 16;
   __device__ __forceinline__ static void to_f32(const raw& v, float f[4]) {
     f[0] = __uint_as_float(v.x);
     f[1] = __uint_as_float(v.y);
@@ -98,13 +112,7 @@ struct Vec4<float> {
 template <>
 struct Vec4<__nv_bfloat16> {
   using raw = uint2;
-  __device__ __forceinline__ static raw load(const __nv_bfloat16* p) {
-    raw v;
-    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];"
-                 : "=r"(v.x), "=r"(v.y)
-                 : "l"(p));
-    return v;
-  }
+  static constexpr int kBytes = 8;
   __device__ __forceinline__ static void to_f32(const raw& v, float f[4]) {
     f[0] = __uint_as_float(v.x << 16);
     f[1] = __uint_as_float(v.x & 0xffff0000u);
@@ -115,13 +123,7 @@ struct Vec4<__nv_bfloat16> {
 template <>
 struct Vec4<__half> {
   using raw = uint2;
-  __device__ __forceinline__ static raw load(const __half* p) {
-    raw v;
-    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];"
-                 : "=r"(v.x), "=r"(v.y)
-                 : "l"(p));
-    return v;
-  }
+  static constexpr int kBytes = 8;
   __device__ __forceinline__ static void to_f32(const raw& v, float f[4]) {
     const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
     const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
@@ -132,16 +134,29 @@ struct Vec4<__half> {
   }
 };
 
+// Asynchronous global -> shared copy of one vector (16 bytes: L2 only; 8
+// bytes: the .ca form, the only one for that size).
+template <int BYTES>
+__device__ __forceinline__ void cp_async(void* smem_dst, const void* gsrc) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(smem_dst);
+  if (BYTES == 16)
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gsrc) : "memory");
+  else
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(d), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // Order-preserving key of an fp32 score (T2:489-494): -0.0 is folded to
 // +0.0, negative values are bit-inverted, the others get the sign bit. The
 // key of an unselectable element is 0 (and the all-ones NaN pattern, whose
 // key is 0, ranks below every other element, exactly where an unselectable
 // one would end up).
-__device__ __forceinline__ uint32_t score_key(float f, bool candidate) {
+__device__ __forceinline__ uint32_t score_key(float f) {
   uint32_t b = __float_as_uint(f);
-  if ((b << 1) == 0u) b = 0u;                       // +-0.0 -> +0.0
-  const uint32_t k = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-  return (candidate && b != 0xff800000u) ? k : 0u;  // -inf is not selectable
+  b = (f == 0.0f) ? 0u : b;                                       // -0.0 -> +0.0
+  const uint32_t k = b ^ ((uint32_t)((int32_t)b >> 31) | 0x80000000u);
+  return b == 0xff800000u ? 0u : k;                               // -inf is not selectable
 }
 
 __device__ __forceinline__ int64_t load_index(const void* p, int64_t i, int bytes) {
@@ -164,235 +179,319 @@ __device__ __forceinline__ int row_candidates(const Params& p, int64_t row) {
   return (int)(last + 1);
 }
 
-// ------------------------------------------------------------ block scans
-// Inclusive prefix sum of `v` over the threads of the CTA in thread order;
-// `tot` receives the CTA total. Uses warp_buf[0..31]; starts and ends with
-// __syncthreads-free warp work around one barrier pair.
-__device__ __forceinline__ uint32_t block_incl_scan(uint32_t v, uint32_t* warp_buf,
-                                                    uint32_t* tot) {
+__device__ __forceinline__ uint32_t bitlen(uint32_t v) { return v ? 32u - __clz(v) : 0u; }
+// Digit width for the range [lo, hi]: the smallest s with (hi - lo) >> s < 512.
+__device__ __forceinline__ uint32_t digit_shift(uint32_t lo, uint32_t hi) {
+  const uint32_t l = bitlen(hi - lo);
+  return l > (uint32_t)kBinBits ? l - kBinBits : 0u;
+}
+
+// Inclusive prefix sum of `v` over the CTA in thread order; `tot` gets the
+// CTA total. Uses buf[0..31] between two barriers.
+__device__ __forceinline__ uint32_t block_incl_scan(uint32_t v, uint32_t* buf, uint32_t* tot) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const uint32_t u = __shfl_up_sync(0xffffffffu, v, o);
     if (lane >= o) v += u;
   }
-  if (lane == 31) warp_buf[warp] = v;
+  if (lane == 31) buf[warp] = v;
   __syncthreads();
   uint32_t before = 0, all = 0;
   for (int w = 0; w < nw; ++w) {
-    const uint32_t x = warp_buf[w];
+    const uint32_t x = buf[w];
     before += w < warp ? x : 0u;
     all += x;
   }
   *tot = all;
-  __syncthreads();  // warp_buf may be reused right after
+  __syncthreads();
   return v + before;
 }
 
-// Result of a threshold search: the bin holding the `need`-th largest key
-// among the histogram's keys, the number of keys in higher bins and in it.
-struct BinHit {
-  uint32_t bin, above, count;
-};
-
-// Every thread owns nbins / T consecutive bins, thread 0 the highest ones.
-// Exactly one thread finds need inside its range (1 <= need <= total).
-__device__ __forceinline__ BinHit find_bin(const uint32_t* hist, int nbins, uint32_t need,
-                                           uint32_t* warp_buf, BinHit* s_hit) {
+// Suffix counts of a 512-bin histogram plus an overflow count `ov` (keys
+// above every bin): F[b] = ov + sum of hist[b..511], F[512] = ov. Returns the
+// bin b with F[b+1] < need <= F[b] (1 <= need <= F[0]). Thread t owns
+// 512 / T consecutive bins, thread 0 the highest ones. Ends with a barrier.
+__device__ __forceinline__ uint32_t suffix_find(const uint32_t* hist, uint32_t ov, uint32_t need,
+                                                uint32_t* F, uint32_t* buf, uint32_t* s_bin) {
   const int T = blockDim.x;
-  const int bpt = nbins / T;
-  const int lo = nbins - (threadIdx.x + 1) * bpt;  // lowest bin of this thread
+  const int bpt = kBins / T;
+  const int lo = kBins - (threadIdx.x + 1) * bpt;  // lowest bin of this thread
   uint32_t local = 0;
   for (int i = 0; i < bpt; ++i) local += hist[lo + i];
   uint32_t tot;
-  const uint32_t incl = block_incl_scan(local, warp_buf, &tot);
-  const uint32_t excl = incl - local;
-  if (excl < need && need <= incl) {
-    uint32_t acc = excl;
-    for (int b = lo + bpt - 1; b >= lo; --b) {
-      const uint32_t c = hist[b];
-      if (acc + c >= need) {
-        *s_hit = BinHit{(uint32_t)b, acc, c};
-        break;
-      }
-      acc += c;
-    }
+  const uint32_t incl = block_incl_scan(local, buf, &tot);
+  uint32_t acc = ov + incl - local;  // keys in bins above this thread's range
+  for (int b = lo + bpt - 1; b >= lo; --b) {
+    const uint32_t c = hist[b];
+    if (acc < need && need <= acc + c) *s_bin = (uint32_t)b;
+    acc += c;
+    F[b] = acc;
   }
+  if (threadIdx.x == 0) F[kBins] = ov;
   __syncthreads();
-  return *s_hit;
+  return *s_bin;
 }
 
 // --------------------------------------------------------------- kernel
-template <typename Tin, int J>
-__global__ void __launch_bounds__(kMaxThreads) dsa_topk_kernel(const Params p) {
-  extern __shared__ __align__(16) uint8_t smem[];
-  const Smem L = smem_layout(p.K);
-  uint32_t* hist = reinterpret_cast<uint32_t*>(smem + L.hist);
-  uint64_t* list = reinterpret_cast<uint64_t*>(smem + L.list);
-  int32_t* outid = reinterpret_cast<int32_t*>(smem + L.outid);
-  __shared__ uint32_t s_warp[32];
-  __shared__ uint32_t s_count;
-  __shared__ BinHit s_hit;
-
+// NT threads per CTA (128, 256 or 512), J vectors per thread. The register
+// budget leaves room for 5 CTAs of 128 threads per SM (2 of 256).
+template <typename Tin, int J, int NT>
+__global__ void __launch_bounds__(NT, NT == 128 ? 5 : NT == 256 ? 2 : 1)
+    dsa_topk_kernel(const Params p) {
   using V = Vec4<Tin>;
   using raw = typename V::raw;
-  const int T = blockDim.x;
+  extern __shared__ __align__(16) uint8_t smem[];
+  constexpr int T = NT;
   const int t = threadIdx.x;
+  const int lane = t & 31, warp = t >> 5, nw = T >> 5;
   const int NB = p.NB;
+  const int nvec = NB >> 2;
   const int K = p.K;
+  const int cap = p.cap;
+  const Smem L = smem_layout(T, J, V::kBytes, K, cap);
+  raw* stage = reinterpret_cast<raw*>(smem + L.stage);
+  uint64_t* cand = reinterpret_cast<uint64_t*>(smem + L.cand);
+  uint64_t* ord = reinterpret_cast<uint64_t*>(smem + L.ord);
+  uint32_t* hist = reinterpret_cast<uint32_t*>(smem + L.hist);
+  uint32_t* F = reinterpret_cast<uint32_t*>(smem + L.F);
+  int32_t* outid = reinterpret_cast<int32_t*>(smem + L.outid);
+  __shared__ uint32_t s_red[2][3][32];
+  __shared__ uint32_t s_buf[32];
+  __shared__ uint32_t s_C;
+  __shared__ uint32_t s_bin;
   const Tin* scores = static_cast<const Tin*>(p.scores);
 
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-  int64_t row = blockIdx.x;
-  raw nxt[J];
-  int n_nxt = 0;
-  auto prefetch = [&](int64_t r) {
-    n_nxt = row_candidates(p, r);
+  auto issue = [&](int64_t r, int n) {
     const Tin* base = scores + r * (int64_t)NB;
 #pragma unroll
     for (int j = 0; j < J; ++j) {
       const int v = j * T + t;
-      if (4 * v < n_nxt) nxt[j] = V::load(base + 4 * (int64_t)v);
+      if (v < nvec && 4 * v < n) cp_async<V::kBytes>(stage + v, base + 4 * (int64_t)v);
     }
+    cp_async_commit();
   };
-  if (row < p.rows) prefetch(row);
 
-  for (; row < p.rows; row += gridDim.x) {
-    // ---- keys of this row (registers), next row's loads in flight
-    const int n = n_nxt;
+  int64_t row = blockIdx.x;
+  const int64_t G = gridDim.x;
+  int n_cur = 0, n_next = 0;
+  if (row < p.rows) {
+    n_cur = row_candidates(p, row);
+    issue(row, n_cur);
+    if (row + G < p.rows) n_next = row_candidates(p, row + G);
+  }
+  int rb = 0;  // reduction buffer parity
+
+  for (; row < p.rows; row += G, rb ^= 1) {
+    const int n = n_cur;
+    // ---- 1. keys of this row (own staged vectors)
+    cp_async_wait_all();
     uint32_t key[J][4];
+    uint32_t mx = 0, nz = 0;
+    const bool full = n == NB;
 #pragma unroll
     for (int j = 0; j < J; ++j) {
       const int v = j * T + t;
       float f[4] = {0.f, 0.f, 0.f, 0.f};
-      if (4 * v < n) V::to_f32(nxt[j], f);
+      const bool in = v < nvec && 4 * v < n;
+      if (in) V::to_f32(stage[v], f);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) key[j][c] = score_key(f[c], 4 * v + c < n);
+      for (int c = 0; c < 4; ++c) {
+        uint32_t k = score_key(f[c]);
+        if (!full) k = (in && 4 * v + c < n) ? k : 0u;
+        else if (!(v < nvec)) k = 0u;
+        key[j][c] = k;
+        mx = max(mx, k);
+        nz += k != 0u ? 1u : 0u;
+      }
     }
-    if (row + gridDim.x < p.rows) prefetch(row + gridDim.x);
+    // the staged vectors are in registers (mx depends on every one of them,
+    // and the empty asm orders that before the copies below): start the next
+    // row's copies into the same buffer
+    asm volatile("" ::"r"(mx), "r"(nz));
+    if (row + G < p.rows) {
+      issue(row + G, n_next);
+      n_cur = n_next;
+      if (row + 2 * G < p.rows) n_next = row_candidates(p, row + 2 * G);
+    }
 
-    // ---- pass 1: histogram of bits 31..20
-    for (int i = t; i < kBins1 / 4; i += T) reinterpret_cast<uint4*>(hist)[i] = make_uint4(0, 0, 0, 0);
-    __syncthreads();
-    uint32_t mine = 0;
+    // ---- 2. block reduction: selectable count, max key, lower bound
+    uint32_t gm = mx;
+    for (int o = 1; o < p.group; o <<= 1) gm = max(gm, __shfl_xor_sync(0xffffffffu, gm, o));
+    uint32_t t0 = p.group > 0 ? gm : 0u;
+    uint32_t wnz = nz, wmx = mx;
 #pragma unroll
-    for (int j = 0; j < J; ++j)
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-        if (key[j][c]) {
-          atomicAdd(&hist[key[j][c] >> 20], 1u);
-          ++mine;
-        }
+    for (int o = 16; o > 0; o >>= 1) {
+      wnz += __shfl_xor_sync(0xffffffffu, wnz, o);
+      wmx = max(wmx, __shfl_xor_sync(0xffffffffu, wmx, o));
+      t0 = min(t0, __shfl_xor_sync(0xffffffffu, t0, o));
+    }
+    if (lane == 0) {
+      s_red[rb][0][warp] = wnz;
+      s_red[rb][1][warp] = wmx;
+      s_red[rb][2][warp] = t0;
+    }
+    if (t == 0) s_C = 0;
+    for (int i = t; i < kBins + 1; i += T) hist[i] = 0;
     __syncthreads();
-    uint32_t total;
-    (void)block_incl_scan(mine, s_warp, &total);
+    uint32_t total = 0, hi = 0, lo = 0xffffffffu;
+    for (int w = 0; w < nw; ++w) {
+      total += s_red[rb][0][w];
+      hi = max(hi, s_red[rb][1][w]);
+      lo = min(lo, s_red[rb][2][w]);
+    }
     const uint32_t need = total < (uint32_t)K ? total : (uint32_t)K;
+    if (total <= (uint32_t)K) lo = 1u;   // every selectable key is an output
+    lo = max(lo, 1u);
 
-    // Selection rule: keys k != 0 with (k >> shift) > prefix, and with
-    // (k >> shift) == prefix either all of them (take_all) or, after the
-    // last digit, the first `ties` of them in block-id order.
-    uint32_t prefix = 0, above = 0;
-    int shift = 32;
-    bool take_all = true;
-    if (need > 0 && need < total) {
-      BinHit h = find_bin(hist, kBins1, need, s_warp, &s_hit);
-      prefix = h.bin;
-      shift = 20;
-      above = h.above;
-      take_all = h.above + h.count == need;
-      for (int pass = 0; pass < 2 && !take_all; ++pass) {
-        const int s2 = 10 - 10 * pass;  // digit bits s2+9 .. s2
-        for (int i = t; i < kBins2 / 4; i += T) reinterpret_cast<uint4*>(hist)[i] = make_uint4(0, 0, 0, 0);
+    if (need > 0) {
+      // ---- 3. compaction of the keys >= lo (refined first if too many)
+      uint32_t C = 0;
+      bool tie_path = false;
+      uint32_t kth = 0, above = 0;
+      for (;;) {
+        uint32_t cnt = 0;
+#pragma unroll
+        for (int j = 0; j < J; ++j)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) cnt += key[j][c] >= lo ? 1u : 0u;
+        uint32_t incl = cnt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t u = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += u;
+        }
+        uint32_t base = 0;
+        if (lane == 31) base = atomicAdd(&s_C, incl);
+        base = __shfl_sync(0xffffffffu, base, 31);
+        uint32_t o = base + incl - cnt;
+        if (o + cnt <= (uint32_t)cap) {
+#pragma unroll
+          for (int j = 0; j < J; ++j)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const uint32_t k = key[j][c];
+              if (k >= lo) {
+                cand[o++] = ((uint64_t)k << 32) | (uint64_t)(0xffffffffu - (uint32_t)(4 * (j * T + t) + c));
+              }
+            }
+        }
         __syncthreads();
+        C = s_C;
+        if (C <= (uint32_t)cap) break;
+
+        // Too many: radix refinement of the bound over the register keys.
+        // Level 0 spans [lo, hi]; each level splits the K-th key's bin of
+        // the previous level into 512 (keys above it counted as overflow).
+        uint32_t s = digit_shift(lo, hi);
+        uint32_t lvl_lo = lo;
+        bool first = true;
+        for (;;) {
+          if (!first)
+            for (int i = t; i < kBins + 1; i += T) hist[i] = 0;
+          if (!first) __syncthreads();
+          first = false;
+#pragma unroll
+          for (int j = 0; j < J; ++j)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const uint32_t k = key[j][c];
+              if (k >= lvl_lo) {
+                const uint32_t d = (k - lvl_lo) >> s;
+                atomicAdd(&hist[d < (uint32_t)kBins ? d : (uint32_t)kBins], 1u);
+              }
+            }
+          __syncthreads();
+          const uint32_t ov = hist[kBins];
+          const uint32_t b = suffix_find(hist, ov, need, F, s_buf, &s_bin);
+          const uint32_t cnt_ge = F[b];
+          above = F[b + 1];
+          lvl_lo += b << s;
+          if (cnt_ge <= (uint32_t)cap) {
+            lo = lvl_lo;
+            break;
+          }
+          if (s == 0) {  // one key value, too many copies of it
+            tie_path = true;
+            kth = lvl_lo;
+            break;
+          }
+          s = s > (uint32_t)kBinBits ? s - kBinBits : 0u;
+          __syncthreads();  // F and s_bin are read above before the next level rewrites them
+        }
+        __syncthreads();
+        if (t == 0) s_C = 0;
+        for (int i = t; i < kBins + 1; i += T) hist[i] = 0;
+        __syncthreads();
+        if (tie_path) break;
+      }
+
+      if (tie_path) {
+        // keys above the K-th key (fewer than need), then the first
+        // need - above copies of it in block-id order (ids 4(jT + t) + c)
+        const uint32_t r = need - above;
 #pragma unroll
         for (int j = 0; j < J; ++j)
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             const uint32_t k = key[j][c];
-            if (k && (k >> shift) == prefix) atomicAdd(&hist[(k >> s2) & (kBins2 - 1)], 1u);
+            if (k > kth) cand[atomicAdd(&s_C, 1u)] =
+                ((uint64_t)k << 32) | (uint64_t)(0xffffffffu - (uint32_t)(4 * (j * T + t) + c));
           }
-        __syncthreads();
-        h = find_bin(hist, kBins2, need - above, s_warp, &s_hit);
-        prefix = (prefix << 10) | h.bin;
-        shift = s2;
-        above += h.above;
-        take_all = above + h.count == need;
-      }
-    }
-    // shift == 32 means "every selectable key" (need == total)
-    const uint32_t ties = need - above;  // keys equal to the full key to take
-
-    // ---- gather the winners into `list` as 64-bit (key, ~id) codes
-    if (t == 0) s_count = 0;
-    __syncthreads();
-    if (need > 0) {
-      uint32_t tie_base = 0;
+        uint32_t eq_base = 0;
 #pragma unroll
-      for (int j = 0; j < J; ++j) {
-        const int v = j * T + t;
-        bool sel[4];
-        uint32_t eq = 0;
+        for (int j = 0; j < J; ++j) {
+          uint32_t e = 0;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const uint32_t k = key[j][c];
-          const uint32_t hi = shift == 32 ? 0u : (k >> shift);
-          sel[c] = k != 0 && (shift == 32 || hi > prefix || (hi == prefix && take_all));
-          eq += (k != 0 && !take_all && hi == prefix) ? 1u : 0u;
-        }
-        if (!take_all) {
-          // Keys equal to the K-th key: the first `ties` in block-id order
-          // (ids 4v+c, v = j*T + t: thread order within one j, j ascending).
+          for (int c = 0; c < 4; ++c) e += key[j][c] == kth ? 1u : 0u;
           uint32_t tot;
-          const uint32_t incl = block_incl_scan(eq, s_warp, &tot);
-          uint32_t pos = tie_base + incl - eq;
+          const uint32_t incl = block_incl_scan(e, s_buf, &tot);
+          uint32_t pos = eq_base + incl - e;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            const uint32_t k = key[j][c];
-            if (k != 0 && (k >> shift) == prefix) {
-              sel[c] = pos < ties;
+            if (key[j][c] == kth) {
+              if (pos < r)
+                cand[atomicAdd(&s_C, 1u)] =
+                    ((uint64_t)kth << 32) | (uint64_t)(0xffffffffu - (uint32_t)(4 * (j * T + t) + c));
               ++pos;
             }
           }
-          tie_base += tot;
+          eq_base += tot;
         }
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          if (sel[c]) {
-            const uint32_t slot = atomicAdd(&s_count, 1u);
-            list[slot] = ((uint64_t)key[j][c] << 32) | (uint64_t)(0xffffffffu - (uint32_t)(4 * v + c));
-          }
-        }
+        __syncthreads();
+        C = s_C;
+        lo = kth;
       }
-    }
-    __syncthreads();
 
-    // ---- rank the winners (codes are unique) and place their ids. Each
-    // winner is compared with all the others by `sub` neighbouring lanes
-    // (need <= T/sub), whose partial counts are summed by shuffles.
-    {
-      uint32_t np2 = 1;
-      while (np2 < need) np2 <<= 1;
-      int sub = (uint32_t)T >= np2 ? T / (int)np2 : 1;
-      if (sub > 32) sub = 32;
-      const int per_round = T / sub;
-      for (uint32_t base = 0; base < need; base += per_round) {
-        const uint32_t i = base + t / sub;
-        const int part = t & (sub - 1);
+      // ---- 4. exact order of the top `need` candidates
+      const uint32_t s = digit_shift(lo, hi);
+      for (uint32_t i = t; i < C; i += T)
+        atomicAdd(&hist[((uint32_t)(cand[i] >> 32) - lo) >> s], 1u);
+      __syncthreads();
+      const uint32_t bstar = suffix_find(hist, 0u, need, F, s_buf, &s_bin);
+      for (uint32_t i = t; i < C; i += T) {
+        const uint64_t code = cand[i];
+        const uint32_t d = ((uint32_t)(code >> 32) - lo) >> s;
+        if (d >= bstar) ord[F[d + 1] + atomicSub(&hist[d], 1u) - 1u] = code;
+      }
+      __syncthreads();
+      const uint32_t E = F[bstar];
+      for (uint32_t i = t; i < E; i += T) {
+        const uint64_t code = ord[i];
+        const uint32_t d = ((uint32_t)(code >> 32) - lo) >> s;
+        const uint32_t s0 = F[d + 1], s1 = F[d];
         uint32_t rank = 0;
-        uint64_t me = 0;
-        if (i < need) {
-          me = list[i];
-          for (uint32_t q = part; q < need; q += sub) rank += list[q] > me ? 1u : 0u;
-        }
-        for (int o = sub >> 1; o > 0; o >>= 1) rank += __shfl_xor_sync(0xffffffffu, rank, o);
-        if (i < need && part == 0) outid[rank] = (int32_t)(0xffffffffu - (uint32_t)me);
+        for (uint32_t q = s0; q < s1; ++q) rank += ord[q] > code ? 1u : 0u;
+        const uint32_t slot = s0 + rank;
+        if (slot < need) outid[slot] = (int32_t)(0xffffffffu - (uint32_t)code);
       }
+      __syncthreads();
     }
-    __syncthreads();
 
-    // ---- outputs: ids and their pages, -1 beyond the winners
+    // ---- 5. outputs: ids and their pages, -1 beyond the winners
     const int64_t b = row / p.HQ;
     for (int k = t; k < K; k += T) {
       const int32_t id = k < (int)need ? outid[k] : -1;
@@ -412,12 +511,11 @@ __global__ void __launch_bounds__(kMaxThreads) dsa_topk_kernel(const Params p) {
       else
         reinterpret_cast<int*>(p.out_pages)[o] = (int)page;
     }
-    // the next row's first histogram write must not overtake this row's reads
-    __syncthreads();
   }
+  cp_async_wait_all();
 }
 
 using KernelFn = void (*)(const Params);
-KernelFn topk_kernel(int scores_dtype, int J);  // dsa_topk.cu
+KernelFn topk_kernel(int scores_dtype, int J, int T);  // dsa_topk.cu
 
 }  // namespace dsa
