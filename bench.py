@@ -694,6 +694,72 @@ def run_topk_reference(args, w, world):
     }), flush=True)
 
 
+def run_pcie(args, rank, world, local):
+    """Host-link ceiling of the end-to-end leg: bare pinned-memory copies of
+    the e2e leg's bytes (x and residual in, residual_out, x_q and x_scale
+    out, for --e2e-stage-rows rows of the workload), both directions at once
+    on two streams, on every rank at the same time. Prints one JSON line:
+    aggregate GB/s of the workload's algorithmic bytes moved at that copy
+    speed (comparable with the e2e value), and the raw copy GB/s per
+    direction. Not the default benchmark."""
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    pg = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+        pg = dist
+    w = CONFIGS[args.config]
+    a, b = shard_rows(w.M, world, rank) if args.scaling == "strong" else (0, w.M)
+    rows = min(args.e2e_stage_rows, b - a)
+    esz = 2
+    h2d = rows * w.D * esz * 2
+    d2h = rows * (w.D * esz + w.D + w.groups * 4)
+    hin = torch.empty(h2d, dtype=torch.uint8, pin_memory=True)
+    hout = torch.empty(d2h, dtype=torch.uint8, pin_memory=True)
+    din = torch.empty(h2d, dtype=torch.uint8, device=dev)
+    dout = torch.empty(d2h, dtype=torch.uint8, device=dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    res = {}
+    for mode in ("h2d", "d2h", "both"):
+        def step():
+            if mode in ("h2d", "both"):
+                with torch.cuda.stream(s_in):
+                    din.copy_(hin, non_blocking=True)
+            if mode in ("d2h", "both"):
+                with torch.cuda.stream(s_out):
+                    hout.copy_(dout, non_blocking=True)
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize(dev)
+        if pg:
+            pg.barrier()
+        t0 = time.perf_counter()
+        n = max(3, args.steps // 10)
+        for _ in range(n):
+            step()
+        torch.cuda.synchronize(dev)
+        dt = torch.tensor([(time.perf_counter() - t0) / n], dtype=torch.float64, device=dev)
+        if pg:
+            pg.all_reduce(dt, op=pg.ReduceOp.MAX)
+        res[mode] = float(dt)
+    if pg:
+        pg.destroy_process_group()
+    if rank != 0:
+        return
+    alg = bytes_per_call(rows, w.D, w.group_size) * world
+    print(json.dumps({
+        "metric": "host-link ceiling of the e2e leg: bare pinned copies on every rank at once",
+        "mode": "pcie", "n_gpus": world, "rows_per_gpu": rows,
+        "h2d_gbs_per_gpu": round(h2d / res["h2d"] / 1e9, 2),
+        "d2h_gbs_per_gpu": round(d2h / res["d2h"] / 1e9, 2),
+        "both_ms": res["both"] * 1e3,
+        "aggregate_copy_gbs_both": round((h2d + d2h) * world / res["both"] / 1e9, 2),
+        "ceiling_algorithmic_gbs": round(alg / res["both"] / 1e9, 2),
+        "timing": "host clock around K copy rounds after a device sync, max over ranks",
+    }), flush=True)
+
+
 def run_latency(args, local):
     """Small-M latency regime (M <= 128, where the reference's launch
     overhead dominates): host microseconds per eager call (the Python
@@ -781,11 +847,12 @@ def main():
     ap.add_argument("--rows", type=int, default=0,
                     help="override the workload's total rows (small cases for ncu captures)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--mode", default="rows", choices=["rows", "tp", "latency", "topk"],
+    ap.add_argument("--mode", default="rows", choices=["rows", "tp", "latency", "topk", "pcie"],
                     help="rows: the operator on row shards (default benchmark); tp: the "
                          "tensor-parallel variant (all-reduce fused with the operator); "
                          "latency: small-M host and device cost per call; topk: the DSA "
-                         "top-k page-table transform (Task 02)")
+                         "top-k page-table transform (Task 02); pcie: host-link ceiling of the "
+                         "e2e leg")
     ap.add_argument("--topk-config", default="t2_nb4096_k128_2x32x512",
                     help="Task 02 workload of --mode topk (topk_workloads.TOPK_CONFIGS)")
     ap.add_argument("--scaling", default=None, choices=["weak", "strong"],
@@ -824,6 +891,9 @@ def main():
         return
     if args.mode == "topk":
         run_topk(args, rank, world, local)
+        return
+    if args.mode == "pcie":
+        run_pcie(args, rank, world, local)
         return
     if args.impl == "reference":
         run_reference_arm(args, w, rank, world)

@@ -78,13 +78,21 @@ void pick_shape(int64_t NB, int* T, int* J) {
   *J = (int)((nvec + *T - 1) / *T);
 }
 
-// Threads per lower-bound group: the largest power of two g <= 32 that
-// still leaves T / g >= K groups (0 when K > T: no bound).
-int pick_group(int T, int K) {
-  if (K > T) return 0;
+// Lower-bound groups: a thread vouches for two keys (its two largest vector
+// maxima) when it holds at least two vectors, else for one (its max); a
+// group of g threads vouches for as many. g = the largest power of two <= 32
+// that leaves vouch * T / g >= K (group 0 when even g = 1 falls short: no
+// bound). A thread whose vectors are masked vouches for keys 0, which turns
+// the bound off for that row (the kernel then takes every selectable key).
+void pick_group(int T, int J, int K, int* group, int* vouch) {
+  *vouch = J >= 2 ? 2 : 1;
+  if (K > *vouch * T) {
+    *group = 0;
+    return;
+  }
   int g = 1;
-  while (g < 32 && T / (2 * g) >= K) g *= 2;
-  return g;
+  while (g < 32 && *vouch * T / (2 * g) >= K) g *= 2;
+  *group = g;
 }
 
 int validate(const dsa_topk_args_t* a) {
@@ -102,6 +110,8 @@ int validate(const dsa_topk_args_t* a) {
   if (a->B > lim || a->H > lim || a->Q > lim) return DSA_ERR_BAD_SHAPE;
   const double rows = (double)a->B * (double)a->H * (double)a->Q;
   if (rows * (double)a->NB > 9.0e18 || rows * (double)a->top_k > 9.0e18) return DSA_ERR_BAD_SHAPE;
+  // rows are indexed in 32 bits on the device (B*H*Q < 2^31)
+  if (rows >= 2147483648.0) return DSA_ERR_UNSUPPORTED;
   return DSA_OK;
 }
 
@@ -123,7 +133,7 @@ const char* dsa_topk_strerror(int status) {
     case DSA_ERR_BAD_DTYPE: return "unsupported dtype (scores fp32/bf16/fp16, indices int32/int64)";
     case DSA_ERR_ALIGNMENT:
       return "misaligned pointer (scores 16-byte aligned, index tensors aligned to their element size)";
-    case DSA_ERR_UNSUPPORTED: return "NB > 16384 is not supported";
+    case DSA_ERR_UNSUPPORTED: return "NB > 16384 or B*H*Q >= 2^31 is not supported";
     case DSA_ERR_CUDA: return "a CUDA runtime call failed";
     case DSA_ERR_BAD_ARGS_SIZE:
       return "argument struct size mismatch (header and library differ) or reserved field not 0";
@@ -196,7 +206,9 @@ int dsa_topk_launch(const dsa_topk_args_t* a, void* stream) {
   p.page_bytes = pb;
   p.blocks_bytes = bb;
   p.cap = cap;
-  p.group = pick_group(T, a->top_k);
+  pick_group(T, J, a->top_k, &p.group, &p.vouch);
+  fast_div_init((uint32_t)p.HQ, &p.hq_mul, &p.hq_shift);
+  fast_div_init((uint32_t)p.Q, &p.q_mul, &p.q_shift);
 
   // Programmatic stream serialisation: this launch may start while the
   // previous kernel in the stream drains; the kernel waits for it

@@ -16,13 +16,16 @@
 // reads only its own vectors, so no CTA barrier guards the staging buffer).
 //
 // Per row, exactly:
-//  1. keys: every score becomes an order-preserving 32-bit key, 0 for a block
-//     that is not selectable. Per-thread max and count of selectable keys.
-//  2. lower bound: threads are grouped so that there are at least K groups;
-//     every group max is a distinct key, so at least K keys are >= the
-//     smallest group max (t0). One block reduction gives the selectable
-//     count, the row max `hi` and t0.
-//  3. compaction: the keys >= t0 (about 470 of 4096 at K = 128 for Gaussian
+//  1. keys: every score becomes an order-preserving 32-bit key (a raw key
+//     first: the sign handling only), 0 for a masked block; per-thread max.
+//  2. lower bound: every thread keeps its two largest vector maxima, so it
+//     holds two distinct keys >= the second one; threads are grouped so that
+//     the groups vouch for at least K keys (two each), and the smallest
+//     group bound t0 has at least K keys >= it. One block reduction gives
+//     the row max `hi` and t0. When t0 is above the raw key of -inf, every key >= t0 is
+//     selectable and K of them exist; otherwise (short or -inf-heavy rows)
+//     the keys are made exact and all selectable keys are candidates.
+//  3. compaction: the keys >= t0 (about 380 of 4096 at K = 128 for Gaussian
 //     scores) are appended to a shared candidate list as 64-bit codes
 //     (key << 32 | ~id), one shared atomic per warp. Codes are unique, so
 //     their order is the exact output order. If more than `cap` keys pass
@@ -46,6 +49,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "dsa_topk.h"
 
 namespace dsa {
@@ -54,7 +59,7 @@ constexpr int kMaxThreads = 512;
 constexpr int kBins = 512;      // histogram digits of 9 bits
 constexpr int kBinBits = 9;
 constexpr int kMaxTopK = 2048;
-constexpr int kMinCap = 1024;   // candidate list capacity (at least K)
+constexpr int kMinCap = 768;    // candidate list capacity (at least K)
 constexpr int64_t kMaxBlocks = 16384;
 
 struct Params {
@@ -75,22 +80,44 @@ struct Params {
   int32_t blocks_bytes;  // out_blocks element size (4 or 8)
   int32_t cap;           // candidate list capacity (>= K)
   int32_t group;         // threads per lower-bound group (power of two <= 32), 0 = no bound
+  int32_t vouch;         // keys each group vouches for (1: its max, 2: its second largest
+                         // vector max); T / group * vouch >= K
+  uint32_t hq_mul, hq_shift;  // row / (H*Q) = fast_div(row, ...)  (rows < 2^31)
+  uint32_t q_mul, q_shift;    // row / Q
 };
 
-// Shared-memory carve-up (dynamic part), identical on host and device.
+// Division of n < 2^31 by a constant d >= 1 with a precomputed multiplier
+// (the round-up method of Granlund and Montgomery, "Division by invariant
+// integers using multiplication", 1994): l = ceil(log2 d),
+// m = floor(2^32 (2^l - d) / d) + 1, n / d = (umulhi(n, m) + n) >> l.
+__host__ inline void fast_div_init(uint32_t d, uint32_t* mul, uint32_t* shift) {
+  uint32_t l = 0;
+  while (l < 32 && (1ull << l) < d) ++l;
+  *mul = (uint32_t)(((1ull << 32) * ((1ull << l) - d)) / d + 1);
+  *shift = l;
+}
+__device__ __forceinline__ uint32_t fast_div(uint32_t n, uint32_t mul, uint32_t shift) {
+  return (__umulhi(n, mul) + n) >> shift;
+}
+
+// Shared-memory carve-up (dynamic part), identical on host and device: two
+// staging buffers for the scores of a row (the current row and the one in
+// flight), the candidate list, histogram and suffix counts. The
+// bin-ordered copy of the candidates (`ord`) reuses the current row's
+// staging buffer once the candidates are compacted (cap codes must fit).
 struct Smem {
-  size_t stage, cand, ord, hist, F, outid, total;
+  size_t stage, stage_bytes, cand, hist, F, total;
 };
 __host__ __device__ inline size_t align16(size_t v) { return (v + 15) / 16 * 16; }
 __host__ __device__ inline Smem smem_layout(int T, int J, int vec_bytes, int K, int cap) {
   Smem L;
   L.stage = 0;
-  L.cand = align16((size_t)T * J * vec_bytes);
-  L.ord = L.cand + (size_t)cap * sizeof(uint64_t);
-  L.hist = L.ord + (size_t)cap * sizeof(uint64_t);
+  L.stage_bytes = align16((size_t)T * J * vec_bytes);
+  if (L.stage_bytes < (size_t)cap * sizeof(uint64_t)) L.stage_bytes = (size_t)cap * sizeof(uint64_t);
+  L.cand = 2 * L.stage_bytes;
+  L.hist = L.cand + (size_t)cap * sizeof(uint64_t);
   L.F = L.hist + align16((kBins + 1) * sizeof(uint32_t));
-  L.outid = L.F + align16((kBins + 1) * sizeof(uint32_t));
-  L.total = L.outid + align16((size_t)K * sizeof(int32_t));
+  L.total = L.F + align16((kBins + 1) * sizeof(uint32_t));
   return L;
 }
 __host__ __device__ inline int candidate_cap(int K) { return K > kMinCap ? K : kMinCap; }
@@ -134,6 +161,10 @@ struct Vec4<__half> {
   }
 };
 
+__device__ __forceinline__ float to_float(float v) { return v; }
+__device__ __forceinline__ float to_float(__nv_bfloat16 v) { return __bfloat162float(v); }
+__device__ __forceinline__ float to_float(__half v) { return __half2float(v); }
+
 // Asynchronous global -> shared copy of one vector (16 bytes: L2 only; 8
 // bytes: the .ca form, the only one for that size).
 template <int BYTES>
@@ -149,14 +180,23 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 
 // Order-preserving key of an fp32 score (T2:489-494): -0.0 is folded to
 // +0.0, negative values are bit-inverted, the others get the sign bit. The
-// key of an unselectable element is 0 (and the all-ones NaN pattern, whose
-// key is 0, ranks below every other element, exactly where an unselectable
-// one would end up).
-__device__ __forceinline__ uint32_t score_key(float f) {
-  uint32_t b = __float_as_uint(f);
-  b = (f == 0.0f) ? 0u : b;                                       // -0.0 -> +0.0
-  const uint32_t k = b ^ ((uint32_t)((int32_t)b >> 31) | 0x80000000u);
-  return b == 0xff800000u ? 0u : k;                               // -inf is not selectable
+// exact key of an unselectable element (masked, or -inf) is 0; the all-ones
+// NaN pattern also has key 0 and ranks below every other element, exactly
+// where an unselectable one would end up.
+//
+// The kernel first works on raw keys (sign handling only): they order like
+// the exact keys except that -0.0 sits one below +0.0 and -inf (raw
+// 0x007fffff) is still nonzero. exact_key() maps a raw key to the exact one.
+constexpr uint32_t kRawNegZero = 0x7fffffffu;  // raw key of -0.0
+constexpr uint32_t kPosZero = 0x80000000u;     // key of +0.0
+constexpr uint32_t kRawNegInf = 0x007fffffu;   // raw key of -inf
+__device__ __forceinline__ uint32_t raw_key(float f) {
+  const uint32_t b = __float_as_uint(f);
+  return b ^ ((uint32_t)((int32_t)b >> 31) | 0x80000000u);
+}
+__device__ __forceinline__ uint32_t fold_zero(uint32_t r) { return r == kRawNegZero ? kPosZero : r; }
+__device__ __forceinline__ uint32_t exact_key(uint32_t r) {
+  return r == kRawNegInf ? 0u : fold_zero(r);
 }
 
 __device__ __forceinline__ int64_t load_index(const void* p, int64_t i, int bytes) {
@@ -166,9 +206,9 @@ __device__ __forceinline__ int64_t load_index(const void* p, int64_t i, int byte
 }
 
 // Candidates of a row: block ids 0..n-1 (T2:161-166).
-__device__ __forceinline__ int row_candidates(const Params& p, int64_t row) {
-  const int64_t b = row / p.HQ;
-  const int64_t q = row - (row / p.Q) * p.Q;
+__device__ __forceinline__ int row_candidates(const Params& p, uint32_t row) {
+  const int64_t b = fast_div(row, p.hq_mul, p.hq_shift);
+  const int64_t q = row - fast_div(row, p.q_mul, p.q_shift) * (uint32_t)p.Q;
   const int64_t pos = load_index(p.q_pos, b * p.Q + q, p.index_bytes);
   const int64_t kv = load_index(p.kv_lens, b, p.index_bytes);
   if (pos < 0 || kv <= 0) return 0;
@@ -209,28 +249,65 @@ __device__ __forceinline__ uint32_t block_incl_scan(uint32_t v, uint32_t* buf, u
 }
 
 // Suffix counts of a 512-bin histogram plus an overflow count `ov` (keys
-// above every bin): F[b] = ov + sum of hist[b..511], F[512] = ov. Returns the
-// bin b with F[b+1] < need <= F[b] (1 <= need <= F[0]). Thread t owns
-// 512 / T consecutive bins, thread 0 the highest ones. Ends with a barrier.
-__device__ __forceinline__ uint32_t suffix_find(const uint32_t* hist, uint32_t ov, uint32_t need,
-                                                uint32_t* F, uint32_t* buf, uint32_t* s_bin) {
-  const int T = blockDim.x;
-  const int bpt = kBins / T;
-  const int lo = kBins - (threadIdx.x + 1) * bpt;  // lowest bin of this thread
-  uint32_t local = 0;
-  for (int i = 0; i < bpt; ++i) local += hist[lo + i];
-  uint32_t tot;
-  const uint32_t incl = block_incl_scan(local, buf, &tot);
-  uint32_t acc = ov + incl - local;  // keys in bins above this thread's range
-  for (int b = lo + bpt - 1; b >= lo; --b) {
-    const uint32_t c = hist[b];
-    if (acc < need && need <= acc + c) *s_bin = (uint32_t)b;
-    acc += c;
-    F[b] = acc;
+// above every bin): F[b] = ov + sum of hist[b..511], F[512] = ov, and the bin
+// b with F[b+1] < need <= F[b] (1 <= need <= F[0]) into *s_bin. Run by one
+// warp: lane l owns the 16 bins 496 - 16 l .. 511 - 16 l (lane 0 the highest).
+// The caller brackets it with CTA barriers.
+__device__ __forceinline__ void suffix_scan_warp(const uint32_t* hist, uint32_t ov, uint32_t need,
+                                                 uint32_t* F, uint32_t* s_bin) {
+  const int lane = threadIdx.x & 31;
+  const int lo = kBins - 16 * (lane + 1);
+  uint32_t h[16];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint4 v = reinterpret_cast<const uint4*>(hist + lo)[q];
+    h[4 * q] = v.x;
+    h[4 * q + 1] = v.y;
+    h[4 * q + 2] = v.z;
+    h[4 * q + 3] = v.w;
   }
-  if (threadIdx.x == 0) F[kBins] = ov;
-  __syncthreads();
-  return *s_bin;
+  uint32_t local = 0;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) local += h[i];
+  uint32_t incl = local;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t u = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += u;
+  }
+  uint32_t acc = ov + incl - local;  // keys in bins above this lane's range
+  uint32_t f[16];
+#pragma unroll
+  for (int i = 15; i >= 0; --i) {
+    if (acc < need && need <= acc + h[i]) *s_bin = (uint32_t)(lo + i);
+    acc += h[i];
+    f[i] = acc;
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    reinterpret_cast<uint4*>(F + lo)[q] = make_uint4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
+  if (lane == 0) F[kBins] = ov;
+}
+
+// out_blocks[row, slot] = id and out_pages[row, slot] = page_table[b, id]
+// (-1 for both when id < 0), T2:170-175.
+__device__ __forceinline__ void write_out(const Params& p, int64_t row, uint32_t slot, int32_t id) {
+  const int64_t o = row * (int64_t)p.K + slot;
+  int64_t page = -1;
+  if (id >= 0) {
+    const int64_t b = fast_div((uint32_t)row, p.hq_mul, p.hq_shift);
+    const int64_t pi = b * (int64_t)p.NB + id;
+    page = p.page_bytes == 8 ? (int64_t)__ldg(reinterpret_cast<const long long*>(p.page_table) + pi)
+                             : (int64_t)__ldg(reinterpret_cast<const int*>(p.page_table) + pi);
+  }
+  if (p.blocks_bytes == 8)
+    reinterpret_cast<long long*>(p.out_blocks)[o] = id;
+  else
+    reinterpret_cast<int*>(p.out_blocks)[o] = id;
+  if (p.page_bytes == 8)
+    reinterpret_cast<long long*>(p.out_pages)[o] = page;
+  else
+    reinterpret_cast<int*>(p.out_pages)[o] = (int)page;
 }
 
 // --------------------------------------------------------------- kernel
@@ -250,13 +327,10 @@ __global__ void __launch_bounds__(NT, NT == 128 ? 5 : NT == 256 ? 2 : 1)
   const int K = p.K;
   const int cap = p.cap;
   const Smem L = smem_layout(T, J, V::kBytes, K, cap);
-  raw* stage = reinterpret_cast<raw*>(smem + L.stage);
   uint64_t* cand = reinterpret_cast<uint64_t*>(smem + L.cand);
-  uint64_t* ord = reinterpret_cast<uint64_t*>(smem + L.ord);
   uint32_t* hist = reinterpret_cast<uint32_t*>(smem + L.hist);
   uint32_t* F = reinterpret_cast<uint32_t*>(smem + L.F);
-  int32_t* outid = reinterpret_cast<int32_t*>(smem + L.outid);
-  __shared__ uint32_t s_red[2][3][32];
+  __shared__ uint32_t s_red[2][4][32];
   __shared__ uint32_t s_buf[32];
   __shared__ uint32_t s_C;
   __shared__ uint32_t s_bin;
@@ -265,13 +339,16 @@ __global__ void __launch_bounds__(NT, NT == 128 ? 5 : NT == 256 ? 2 : 1)
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-  auto issue = [&](int64_t r, int n) {
-    const Tin* base = scores + r * (int64_t)NB;
+  auto stage_buf = [&](int parity) {
+    return reinterpret_cast<raw*>(smem + L.stage + (size_t)parity * L.stage_bytes);
+  };
+  auto issue = [&](int64_t r, int n, int parity) {
+    const Tin* base = scores + r * (int64_t)NB + 4 * t;
+    raw* st = stage_buf(parity) + t;
+    const int nv = (n + 3) >> 2;  // vectors holding candidates (nv <= nvec)
 #pragma unroll
-    for (int j = 0; j < J; ++j) {
-      const int v = j * T + t;
-      if (v < nvec && 4 * v < n) cp_async<V::kBytes>(stage + v, base + 4 * (int64_t)v);
-    }
+    for (int j = 0; j < J; ++j)
+      if (j * T + t < nv) cp_async<V::kBytes>(st + j * T, base + 4 * j * T);
     cp_async_commit();
   };
 
@@ -279,85 +356,141 @@ __global__ void __launch_bounds__(NT, NT == 128 ? 5 : NT == 256 ? 2 : 1)
   const int64_t G = gridDim.x;
   int n_cur = 0, n_next = 0;
   if (row < p.rows) {
-    n_cur = row_candidates(p, row);
-    issue(row, n_cur);
-    if (row + G < p.rows) n_next = row_candidates(p, row + G);
+    n_cur = row_candidates(p, (uint32_t)row);
+    issue(row, n_cur, 0);
+    if (row + G < p.rows) n_next = row_candidates(p, (uint32_t)(row + G));
   }
-  int rb = 0;  // reduction buffer parity
+  int rb = 0;  // parity: reduction buffer and staging buffer of this row
 
   for (; row < p.rows; row += G, rb ^= 1) {
     const int n = n_cur;
-    // ---- 1. keys of this row (own staged vectors)
+    const raw* stage = stage_buf(rb);
+    // bin-ordered candidates, in this row's staging buffer once it is consumed
+    uint64_t* ord = reinterpret_cast<uint64_t*>(smem + L.stage + (size_t)rb * L.stage_bytes);
+    // ---- 1. raw keys of this row (own staged vectors), 0 when masked
     cp_async_wait_all();
     uint32_t key[J][4];
-    uint32_t mx = 0, nz = 0;
-    const bool full = n == NB;
+    uint32_t mx = 0, mx2 = 0;  // largest and second largest of the vector maxima
+    {
+      const int nfv = n >> 2;  // vectors whose four blocks are all candidates
 #pragma unroll
-    for (int j = 0; j < J; ++j) {
-      const int v = j * T + t;
-      float f[4] = {0.f, 0.f, 0.f, 0.f};
-      const bool in = v < nvec && 4 * v < n;
-      if (in) V::to_f32(stage[v], f);
+      for (int j = 0; j < J; ++j) {
+        const int v = j * T + t;
+        if (v < nfv) {  // warp-uniform except in the warp holding the row's end
+          float f[4];
+          V::to_f32(stage[v], f);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t k = score_key(f[c]);
-        if (!full) k = (in && 4 * v + c < n) ? k : 0u;
-        else if (!(v < nvec)) k = 0u;
-        key[j][c] = k;
-        mx = max(mx, k);
-        nz += k != 0u ? 1u : 0u;
+          for (int c = 0; c < 4; ++c) key[j][c] = raw_key(f[c]);
+        } else {
+          float f[4] = {0.f, 0.f, 0.f, 0.f};
+          if (v == nfv && 4 * v < n) V::to_f32(stage[v], f);
+#pragma unroll
+          for (int c = 0; c < 4; ++c) key[j][c] = 4 * v + c < n ? raw_key(f[c]) : 0u;
+        }
+        const uint32_t vm = max(max(key[j][0], key[j][1]), max(key[j][2], key[j][3]));
+        mx2 = max(mx2, min(mx, vm));
+        mx = max(mx, vm);
       }
     }
-    // the staged vectors are in registers (mx depends on every one of them,
-    // and the empty asm orders that before the copies below): start the next
-    // row's copies into the same buffer
-    asm volatile("" ::"r"(mx), "r"(nz));
-    if (row + G < p.rows) {
-      issue(row + G, n_next);
-      n_cur = n_next;
-      if (row + 2 * G < p.rows) n_next = row_candidates(p, row + 2 * G);
+    // ---- 2. block reduction: max raw key and the lower bound t0. A thread
+    // holds at least two keys >= mx2 (the maxima of two vectors); a group of
+    // threads at least two keys >= the second largest of its members' (mx,
+    // mx2) pairs. With T / group * 2 >= K groups' worth of distinct keys, at
+    // least K keys are >= t0 = the smallest group's second largest.
+    uint32_t g1 = mx, g2 = mx2;
+    for (int o = 1; o < p.group; o <<= 1) {
+      const uint32_t b1 = __shfl_xor_sync(0xffffffffu, g1, o);
+      const uint32_t b2 = __shfl_xor_sync(0xffffffffu, g2, o);
+      g2 = max(min(g1, b1), max(g2, b2));
+      g1 = max(g1, b1);
     }
-
-    // ---- 2. block reduction: selectable count, max key, lower bound
-    uint32_t gm = mx;
-    for (int o = 1; o < p.group; o <<= 1) gm = max(gm, __shfl_xor_sync(0xffffffffu, gm, o));
-    uint32_t t0 = p.group > 0 ? gm : 0u;
-    uint32_t wnz = nz, wmx = mx;
+    uint32_t t0 = p.group > 0 ? (p.vouch == 2 ? g2 : g1) : 0u;
+    uint32_t wmx = mx;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-      wnz += __shfl_xor_sync(0xffffffffu, wnz, o);
       wmx = max(wmx, __shfl_xor_sync(0xffffffffu, wmx, o));
       t0 = min(t0, __shfl_xor_sync(0xffffffffu, t0, o));
     }
     if (lane == 0) {
-      s_red[rb][0][warp] = wnz;
       s_red[rb][1][warp] = wmx;
       s_red[rb][2][warp] = t0;
     }
     if (t == 0) s_C = 0;
     for (int i = t; i < kBins + 1; i += T) hist[i] = 0;
     __syncthreads();
-    uint32_t total = 0, hi = 0, lo = 0xffffffffu;
+    // The next row's copies go to the other staging buffer. It last held the
+    // previous row's scores and bin-ordered candidates, which every thread
+    // has finished reading: all of them have passed the barrier above.
+    if (row + G < p.rows) {
+      issue(row + G, n_next, rb ^ 1);
+      n_cur = n_next;
+      if (row + 2 * G < p.rows) n_next = row_candidates(p, (uint32_t)(row + 2 * G));
+    }
+    uint32_t hi = 0, lo = 0xffffffffu;
     for (int w = 0; w < nw; ++w) {
-      total += s_red[rb][0][w];
       hi = max(hi, s_red[rb][1][w]);
       lo = min(lo, s_red[rb][2][w]);
     }
-    const uint32_t need = total < (uint32_t)K ? total : (uint32_t)K;
-    if (total <= (uint32_t)K) lo = 1u;   // every selectable key is an output
-    lo = max(lo, 1u);
+    uint32_t need;
+    bool exact = false;  // keys in registers are exact keys
+    if (lo > kRawNegInf) {
+      // Fast path: every group max is a selectable key, so at least K
+      // selectable keys are >= lo, and every raw key >= lo is selectable.
+      need = (uint32_t)K;
+      if (lo == kPosZero) lo = kRawNegZero;  // -0.0 ranks with +0.0
+      hi = fold_zero(hi);
+    } else {
+      // No usable bound (a group holds no selectable key): exact keys, the
+      // selectable count and the exact max, then every selectable key is a
+      // candidate.
+      uint32_t nz = 0, ex = 0;
+#pragma unroll
+      for (int j = 0; j < J; ++j)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          key[j][c] = exact_key(key[j][c]);
+          nz += key[j][c] != 0u ? 1u : 0u;
+          ex = max(ex, key[j][c]);
+        }
+      exact = true;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        nz += __shfl_xor_sync(0xffffffffu, nz, o);
+        ex = max(ex, __shfl_xor_sync(0xffffffffu, ex, o));
+      }
+      if (lane == 0) {
+        s_red[rb][0][warp] = nz;
+        s_red[rb][3][warp] = ex;
+      }
+      __syncthreads();
+      uint32_t total = 0;
+      hi = 0;
+      for (int w = 0; w < nw; ++w) {
+        total += s_red[rb][0][w];
+        hi = max(hi, s_red[rb][3][w]);
+      }
+      need = total < (uint32_t)K ? total : (uint32_t)K;
+      lo = 1u;
+      // s_red[rb] is rewritten two rows from now, after this row's barriers
+    }
 
     if (need > 0) {
-      // ---- 3. compaction of the keys >= lo (refined first if too many)
+      // ---- 3. compaction of the keys >= lo (refined first if too many);
+      // codes carry the exact key (the only raw key >= lo that differs from
+      // its exact key is -0.0)
       uint32_t C = 0;
       bool tie_path = false;
       uint32_t kth = 0, above = 0;
+      uint32_t s = 0;  // digit shift of the exact stage: (key - lo) >> s < 512
       for (;;) {
-        uint32_t cnt = 0;
+        s = digit_shift(lo, hi);
+        // bit 4j + c of `mask`: key[j][c] >= lo (J * 4 <= 32 keys)
+        uint32_t mask = 0;
 #pragma unroll
         for (int j = 0; j < J; ++j)
 #pragma unroll
-          for (int c = 0; c < 4; ++c) cnt += key[j][c] >= lo ? 1u : 0u;
+          for (int c = 0; c < 4; ++c) mask |= key[j][c] >= lo ? 1u << (4 * j + c) : 0u;
+        const uint32_t cnt = __popc(mask);
         uint32_t incl = cnt;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -369,57 +502,77 @@ __global__ void __launch_bounds__(NT, NT == 128 ? 5 : NT == 256 ? 2 : 1)
         base = __shfl_sync(0xffffffffu, base, 31);
         uint32_t o = base + incl - cnt;
         if (o + cnt <= (uint32_t)cap) {
-#pragma unroll
-          for (int j = 0; j < J; ++j)
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              const uint32_t k = key[j][c];
-              if (k >= lo) {
-                cand[o++] = ((uint64_t)k << 32) | (uint64_t)(0xffffffffu - (uint32_t)(4 * (j * T + t) + c));
-              }
+          // the candidate's score is re-read from the staging buffer; its
+          // exact key is the raw key with -0.0 folded (the mask holds no
+          // masked, -inf or key-0 element)
+          const Tin* sv = reinterpret_cast<const Tin*>(stage) + 4 * t;
+          const uint32_t nid = 0xffffffffu - 4u * (uint32_t)t;  // ~id of this thread's block 0
+          auto append = [&](auto fold) {
+            while (mask) {
+              const int i = __ffs(mask) - 1;
+              mask &= mask - 1;
+              const int off = (i >> 2) * (4 * T) + (i & 3);  // id - 4t
+              uint32_t k = raw_key(to_float(sv[off]));
+              if (decltype(fold)::value) k = fold_zero(k);
+              cand[o++] = ((uint64_t)k << 32) | (uint64_t)(nid - (uint32_t)off);
+              atomicAdd(&hist[(k - lo) >> s], 1u);
             }
+          };
+          if (lo <= kPosZero)
+            append(std::true_type{});
+          else
+            append(std::false_type{});
         }
         __syncthreads();
         C = s_C;
         if (C <= (uint32_t)cap) break;
 
-        // Too many: radix refinement of the bound over the register keys.
-        // Level 0 spans [lo, hi]; each level splits the K-th key's bin of
-        // the previous level into 512 (keys above it counted as overflow).
-        uint32_t s = digit_shift(lo, hi);
+        // Too many: radix refinement of the bound over the register keys
+        // (made exact first, so that -0.0 and +0.0 are one value). Level 0
+        // spans [lo, hi]; each level splits the K-th key's bin of the
+        // previous level into 512 (keys above it counted as overflow).
+        if (!exact) {
+#pragma unroll
+          for (int j = 0; j < J; ++j)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) key[j][c] = exact_key(key[j][c]);
+          exact = true;
+          lo = fold_zero(lo);
+        }
+        uint32_t sr = digit_shift(lo, hi);
         uint32_t lvl_lo = lo;
-        bool first = true;
         for (;;) {
-          if (!first)
-            for (int i = t; i < kBins + 1; i += T) hist[i] = 0;
-          if (!first) __syncthreads();
-          first = false;
+          // (the failed compaction above, or the previous level, counted
+          // into hist; every thread has read it since the last barrier)
+          for (int i = t; i < kBins + 1; i += T) hist[i] = 0;
+          __syncthreads();
 #pragma unroll
           for (int j = 0; j < J; ++j)
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
               const uint32_t k = key[j][c];
               if (k >= lvl_lo) {
-                const uint32_t d = (k - lvl_lo) >> s;
+                const uint32_t d = (k - lvl_lo) >> sr;
                 atomicAdd(&hist[d < (uint32_t)kBins ? d : (uint32_t)kBins], 1u);
               }
             }
           __syncthreads();
-          const uint32_t ov = hist[kBins];
-          const uint32_t b = suffix_find(hist, ov, need, F, s_buf, &s_bin);
+          if (warp == 0) suffix_scan_warp(hist, hist[kBins], need, F, &s_bin);
+          __syncthreads();
+          const uint32_t b = s_bin;
           const uint32_t cnt_ge = F[b];
           above = F[b + 1];
-          lvl_lo += b << s;
+          lvl_lo += b << sr;
           if (cnt_ge <= (uint32_t)cap) {
             lo = lvl_lo;
             break;
           }
-          if (s == 0) {  // one key value, too many copies of it
+          if (sr == 0) {  // one key value, too many copies of it
             tie_path = true;
             kth = lvl_lo;
             break;
           }
-          s = s > (uint32_t)kBinBits ? s - kBinBits : 0u;
+          sr = sr > (uint32_t)kBinBits ? sr - kBinBits : 0u;
           __syncthreads();  // F and s_bin are read above before the next level rewrites them
         }
         __syncthreads();
@@ -433,13 +586,18 @@ __global__ void __launch_bounds__(NT, NT == 128 ? 5 : NT == 256 ? 2 : 1)
         // keys above the K-th key (fewer than need), then the first
         // need - above copies of it in block-id order (ids 4(jT + t) + c)
         const uint32_t r = need - above;
+        lo = kth;
+        s = digit_shift(lo, hi);
 #pragma unroll
         for (int j = 0; j < J; ++j)
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             const uint32_t k = key[j][c];
-            if (k > kth) cand[atomicAdd(&s_C, 1u)] =
-                ((uint64_t)k << 32) | (uint64_t)(0xffffffffu - (uint32_t)(4 * (j * T + t) + c));
+            if (k > kth) {
+              cand[atomicAdd(&s_C, 1u)] =
+                  ((uint64_t)k << 32) | (uint64_t)(0xffffffffu - (uint32_t)(4 * (j * T + t) + c));
+              atomicAdd(&hist[(k - lo) >> s], 1u);
+            }
           }
         uint32_t eq_base = 0;
 #pragma unroll
@@ -453,9 +611,11 @@ __global__ void __launch_bounds__(NT, NT == 128 ? 5 : NT == 256 ? 2 : 1)
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             if (key[j][c] == kth) {
-              if (pos < r)
+              if (pos < r) {
                 cand[atomicAdd(&s_C, 1u)] =
                     ((uint64_t)kth << 32) | (uint64_t)(0xffffffffu - (uint32_t)(4 * (j * T + t) + c));
+                atomicAdd(&hist[0], 1u);
+              }
               ++pos;
             }
           }
@@ -463,21 +623,21 @@ __global__ void __launch_bounds__(NT, NT == 128 ? 5 : NT == 256 ? 2 : 1)
         }
         __syncthreads();
         C = s_C;
-        lo = kth;
       }
 
-      // ---- 4. exact order of the top `need` candidates
-      const uint32_t s = digit_shift(lo, hi);
-      for (uint32_t i = t; i < C; i += T)
-        atomicAdd(&hist[((uint32_t)(cand[i] >> 32) - lo) >> s], 1u);
+      // ---- 4. exact order of the top `need` candidates (their digit
+      // histogram was counted during the compaction)
+      if (warp == 0) suffix_scan_warp(hist, 0u, need, F, &s_bin);
       __syncthreads();
-      const uint32_t bstar = suffix_find(hist, 0u, need, F, s_buf, &s_bin);
+      const uint32_t bstar = s_bin;
       for (uint32_t i = t; i < C; i += T) {
         const uint64_t code = cand[i];
         const uint32_t d = ((uint32_t)(code >> 32) - lo) >> s;
         if (d >= bstar) ord[F[d + 1] + atomicSub(&hist[d], 1u) - 1u] = code;
       }
       __syncthreads();
+      // ---- 5. each winner's slot = its segment start + its rank inside the
+      // segment; the thread that finds it writes the id and the page
       const uint32_t E = F[bstar];
       for (uint32_t i = t; i < E; i += T) {
         const uint64_t code = ord[i];
@@ -486,31 +646,11 @@ __global__ void __launch_bounds__(NT, NT == 128 ? 5 : NT == 256 ? 2 : 1)
         uint32_t rank = 0;
         for (uint32_t q = s0; q < s1; ++q) rank += ord[q] > code ? 1u : 0u;
         const uint32_t slot = s0 + rank;
-        if (slot < need) outid[slot] = (int32_t)(0xffffffffu - (uint32_t)code);
+        if (slot < need) write_out(p, row, slot, (int32_t)(0xffffffffu - (uint32_t)code));
       }
-      __syncthreads();
     }
-
-    // ---- 5. outputs: ids and their pages, -1 beyond the winners
-    const int64_t b = row / p.HQ;
-    for (int k = t; k < K; k += T) {
-      const int32_t id = k < (int)need ? outid[k] : -1;
-      const int64_t o = row * (int64_t)K + k;
-      int64_t page = -1;
-      if (id >= 0) {
-        const int64_t pi = b * (int64_t)NB + id;
-        page = p.page_bytes == 8 ? (int64_t)__ldg(reinterpret_cast<const long long*>(p.page_table) + pi)
-                                 : (int64_t)__ldg(reinterpret_cast<const int*>(p.page_table) + pi);
-      }
-      if (p.blocks_bytes == 8)
-        reinterpret_cast<long long*>(p.out_blocks)[o] = id;
-      else
-        reinterpret_cast<int*>(p.out_blocks)[o] = id;
-      if (p.page_bytes == 8)
-        reinterpret_cast<long long*>(p.out_pages)[o] = page;
-      else
-        reinterpret_cast<int*>(p.out_pages)[o] = (int)page;
-    }
+    // slots beyond the selectable count
+    for (int k = (int)need + t; k < K; k += T) write_out(p, row, (uint32_t)k, -1);
   }
   cp_async_wait_all();
 }

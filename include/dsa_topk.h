@@ -51,7 +51,7 @@ enum dsa_topk_status {
     DSA_ERR_BAD_DTYPE = 4,      /* unsupported dtype                             */
     DSA_ERR_ALIGNMENT = 5,      /* scores not 16-byte aligned, or an index tensor
                                    not aligned to its element size               */
-    DSA_ERR_UNSUPPORTED = 6,    /* NB > 16384                                    */
+    DSA_ERR_UNSUPPORTED = 6,    /* NB > 16384, or B*H*Q >= 2^31                  */
     DSA_ERR_CUDA = 7,           /* a CUDA runtime call failed                    */
     DSA_ERR_BAD_ARGS_SIZE = 8   /* struct_size mismatch or reserved field not 0  */
 };

@@ -151,6 +151,7 @@ def _args(**kw):
     (dict(page_dtype=7), L.ERR_BAD_DTYPE),
     (dict(NB=32768), L.ERR_UNSUPPORTED),
     (dict(B=1 << 30, H=1 << 30, Q=1 << 30), L.ERR_BAD_SHAPE),
+    (dict(B=1 << 16, H=1 << 15, Q=1, NB=4), L.ERR_UNSUPPORTED),
     (dict(scores=0), L.ERR_NULL_POINTER),
     (dict(out_pages=0), L.ERR_NULL_POINTER),
     (dict(scores=0x10008), L.ERR_ALIGNMENT),
