@@ -493,8 +493,14 @@ def run_tp(args, w, rank, world, local):
         dist.all_reduce(xr)
         fused_add_rmsnorm_group_quant(xr, r, g, ro, no, q, s, w.eps, G, ue8m0=w.ue8m0)
 
+    def fused_kernel_w1():
+        op(M, r, g, w.eps, ue8m0=w.ue8m0, _fused_at_world1=True)
+
+    arms = [("fused", fused), ("nccl_allreduce_then_kernel", unfused)]
+    if world == 1:  # the default routes world 1 to the single-GPU kernel
+        arms.append(("fused_allreduce_kernel_forced_at_world1", fused_kernel_w1))
     res = {}
-    for name, f in (("fused", fused), ("nccl_allreduce_then_kernel", unfused)):
+    for name, f in arms:
         for _ in range(args.warmup):
             f()
         torch.cuda.synchronize(dev)

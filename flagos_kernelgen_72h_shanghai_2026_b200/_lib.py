@@ -16,6 +16,7 @@ from ._build import LIB_PATH
 DTYPE_BF16, DTYPE_FP16, DTYPE_FP32, DTYPE_INT8, DTYPE_E4M3 = 0, 1, 2, 3, 4
 FLAG_UE8M0 = 1
 FLAG_SCALE_COLUMN_MAJOR = 2
+FLAG_AR_KERNEL_AT_WORLD1 = 4
 FLAG_TEST_FORCE_TIMEOUT = 1 << 30  # test only, see include/farq.h
 
 # enum farq_status

@@ -485,11 +485,18 @@ __global__ void __launch_bounds__(NT, NT == 128 ? 5 : NT == 256 ? 2 : 1)
       for (;;) {
         s = digit_shift(lo, hi);
         // bit 4j + c of `mask`: key[j][c] >= lo (J * 4 <= 32 keys)
-        uint32_t mask = 0;
+        // (per-vector nibbles first, then combined pairwise: no 32-long
+        // dependency chain through one register)
+        uint32_t nib[J];
 #pragma unroll
         for (int j = 0; j < J; ++j)
+          nib[j] = (key[j][0] >= lo ? 1u : 0u) | (key[j][1] >= lo ? 2u : 0u) |
+                   (key[j][2] >= lo ? 4u : 0u) | (key[j][3] >= lo ? 8u : 0u);
 #pragma unroll
-          for (int c = 0; c < 4; ++c) mask |= key[j][c] >= lo ? 1u << (4 * j + c) : 0u;
+        for (int w = 1; w < J; w *= 2)
+#pragma unroll
+          for (int j = 0; j + w < J; j += 2 * w) nib[j] |= nib[j + w] << (4 * w);
+        uint32_t mask = nib[0];
         const uint32_t cnt = __popc(mask);
         uint32_t incl = cnt;
 #pragma unroll

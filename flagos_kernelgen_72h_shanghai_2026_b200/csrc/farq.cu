@@ -379,6 +379,32 @@ int farq_ar_launch(const farq_ar_args_t* a, void* stream) {
   if (with_norm && !is_float_out(a->norm_out_dtype)) return FARQ_ERR_BAD_DTYPE;
   if (M == 0) return FARQ_OK;
   if (!a->residual || !a->gamma) return FARQ_ERR_NULL_POINTER;
+  if (W == 1 && !(a->flags & FARQ_FLAG_AR_KERNEL_AT_WORLD1)) {
+    // One rank: the all-reduce is the identity (x = partial[0] exactly), so
+    // the single-GPU kernel does the whole call (with its early L2 prefetch
+    // and dependent launch); no signal words are used.
+    farq_args_t f = {};
+    f.struct_size = sizeof(farq_args_t);
+    f.x_dtype = a->x_dtype;
+    f.gamma_dtype = a->gamma_dtype;
+    f.residual_out_dtype = a->x_dtype;
+    f.norm_out_dtype = a->norm_out_dtype;
+    f.q_dtype = a->q_dtype;
+    f.flags = a->flags & (FARQ_FLAG_UE8M0 | FARQ_FLAG_TEST_FORCE_TIMEOUT);
+    f.group_size = G;
+    f.M = M;
+    f.D = D;
+    f.eps = a->eps;
+    f.x = a->partial[0];
+    f.residual = a->residual;
+    f.gamma = a->gamma;
+    f.residual_out = a->residual_out[0];
+    f.norm_out = a->norm_out[0];
+    f.x_q = a->x_q[0];
+    f.x_scale = a->x_scale[0];
+    f.status = a->status;
+    return farq_launch(&f, stream);
+  }
   if (!aligned(a->residual, 16) || !aligned(a->gamma, 16)) return FARQ_ERR_ALIGNMENT;
   for (int k = 0; k < W; ++k) {
     if (!a->partial[k] || !a->residual_out[k] || !a->x_q[k] || !a->x_scale[k] || !a->signal[k] ||

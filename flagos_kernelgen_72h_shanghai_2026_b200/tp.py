@@ -20,6 +20,7 @@ kernel's cross-rank waits are bounded (2 s) and report through ``status``.
 from __future__ import annotations
 
 import ctypes
+import os
 
 import torch
 
@@ -109,6 +110,11 @@ class TPFusedNormQuant:
             layout[name] = off
             off += _up(nbytes)
         self._layout = layout
+        # The kernel reads and writes peers with plain unicast accesses; the
+        # arena is not bound to an NVLink multicast object (nothing here uses
+        # multimem, and a rank that exits while its memory is bound to one
+        # can fault the other ranks' GPUs).
+        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
         self._arena = symm.empty(off, dtype=torch.uint8, device=self.device)
         self._arena[layout["signal"]: layout["signal"] + SIGNAL_WORDS * 4].zero_()
         torch.cuda.synchronize(self.device)
@@ -163,7 +169,7 @@ class TPFusedNormQuant:
 
     def __call__(self, M: int, residual: torch.Tensor, gamma: torch.Tensor, eps: float, *,
                  ue8m0: bool = False, status: torch.Tensor | None = None,
-                 _test_force_timeout: bool = False):
+                 _test_force_timeout: bool = False, _fused_at_world1: bool = False):
         """x = sum over ranks of partial_buffer(M); returns the replicated
         (residual_out, norm_out, x_q, x_scale) of the operator on x."""
         if not 0 <= M <= self.M:
@@ -177,8 +183,9 @@ class TPFusedNormQuant:
         self.epoch += 1
         a = self._args
         a.gamma_dtype = _DT[gamma.dtype]
-        a.flags = (_lib.FLAG_UE8M0 if ue8m0 else 0) | (
-            _lib.FLAG_TEST_FORCE_TIMEOUT if _test_force_timeout else 0)
+        a.flags = ((_lib.FLAG_UE8M0 if ue8m0 else 0)
+                   | (_lib.FLAG_TEST_FORCE_TIMEOUT if _test_force_timeout else 0)
+                   | (_lib.FLAG_AR_KERNEL_AT_WORLD1 if _fused_at_world1 else 0))
         a.epoch = self.epoch & 0xFFFFFFFF
         a.M = M
         a.eps = float(eps)

@@ -57,6 +57,10 @@ enum farq_flags {
      * ld = x_scale_row_stride (0 = M). No reference counterpart: the reference
      * writes [M, D/G] row-major only (task01…py:1112). */
     FARQ_FLAG_SCALE_COLUMN_MAJOR = 2,
+    /* farq_ar_launch only: at world 1 the all-reduce is the identity and the
+     * call runs the single-GPU kernel (x = partial[0]); this flag runs the
+     * fused all-reduce kernel at world 1 too (tests of that kernel on one GPU). */
+    FARQ_FLAG_AR_KERNEL_AT_WORLD1 = 4,
     /* Test only: the first row team of every CTA waits for a slot sequence
      * value that is never written, with every device wait limited to 1 ms,
      * so the bounded-wait path (status word, drained copies, clean exit) can
@@ -222,7 +226,8 @@ typedef struct farq_ar_args {
     int32_t  gamma_dtype;          /* BF16 | FP16 | FP32                       */
     int32_t  norm_out_dtype;       /* BF16 | FP16 | FP32 (ignored if no norm_out) */
     int32_t  q_dtype;              /* INT8 | E4M3                              */
-    int32_t  flags;                /* FARQ_FLAG_UE8M0; FARQ_FLAG_TEST_FORCE_TIMEOUT
+    int32_t  flags;                /* FARQ_FLAG_UE8M0; FARQ_FLAG_AR_KERNEL_AT_WORLD1;
+                                      FARQ_FLAG_TEST_FORCE_TIMEOUT
                                       makes the start barrier wait (1 ms) for
                                       an epoch no rank signals (tests only)    */
     int32_t  group_size;

@@ -23,7 +23,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, M, D, q):
+def _worker(rank, world, port, M, D, q, fused_at_world1=False):
     try:
         sys.path.insert(0, ROOT)
         sys.path.insert(0, os.path.join(ROOT, "tests"))
@@ -44,7 +44,8 @@ def _worker(rank, world, port, M, D, q):
             residual = (2 * torch.randn(M, D, generator=gen)).to(torch.bfloat16)
             gamma = (1 + 0.1 * torch.randn(D, generator=gen)).to(torch.bfloat16)
             op.partial_buffer(M).copy_(parts[rank])
-            ro, no, xq, xs = op(M, residual.to(dev), gamma.to(dev), 1e-6, status=status)
+            ro, no, xq, xs = op(M, residual.to(dev), gamma.to(dev), 1e-6, status=status,
+                                _fused_at_world1=fused_at_world1)
             torch.cuda.synchronize(dev)
             x = parts[0].float()
             for p in parts[1:]:
@@ -57,11 +58,13 @@ def _worker(rank, world, port, M, D, q):
         if world == 1:
             # a cross-rank wait that nothing satisfies (test-only flag, 1 ms
             # limit) reports through the status word; the next call is exact
-            op(M, residual.to(dev), gamma.to(dev), 1e-6, status=status, _test_force_timeout=True)
+            op(M, residual.to(dev), gamma.to(dev), 1e-6, status=status, _test_force_timeout=True,
+               _fused_at_world1=fused_at_world1)
             torch.cuda.synchronize(dev)
             assert int(status.item()) == 9  # FARQ_ERR_DEVICE_TIMEOUT
             status.zero_()
-            ro, no, xq, xs = op(M, residual.to(dev), gamma.to(dev), 1e-6, status=status)
+            ro, no, xq, xs = op(M, residual.to(dev), gamma.to(dev), 1e-6, status=status,
+                                _fused_at_world1=fused_at_world1)
             torch.cuda.synchronize(dev)
             assert int(status.item()) == 0
             got = dict(residual_out=ro.cpu(), norm_out=no.cpu(), x_q=xq.cpu(), x_scale=xs.cpu())
@@ -73,11 +76,12 @@ def _worker(rank, world, port, M, D, q):
         q.put((rank, traceback.format_exc()))
 
 
-def _run(world, M, D):
+def _run(world, M, D, fused_at_world1=False):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, M, D, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, M, D, q, fused_at_world1))
+             for r in range(world)]
     for p in procs:
         p.start()
     results = {}
@@ -95,7 +99,14 @@ def _run(world, M, D):
 
 
 def test_tp_fused_world1(cuda_dev):
+    """World 1 runs the single-GPU kernel (the all-reduce is the identity)."""
     _run(1, 333, 7168)
+
+
+def test_tp_fused_kernel_at_world1(cuda_dev):
+    """The fused all-reduce kernel itself, forced at world 1 (its only form a
+    one-GPU box can run): two calls and the bounded start-barrier wait."""
+    _run(1, 333, 7168, fused_at_world1=True)
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
