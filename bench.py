@@ -635,7 +635,9 @@ def run_topk(args, rank, world, local):
         "l2": f"inputs larger than L2: {nsets} rotating score set(s) of {per / 1e6:.0f} MB",
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
                      "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                     "traffic": None},
+                     "traffic": profiled_topk_traffic(w.name),
+                     "traffic_source": "DRAM read + write of one ncu-captured launch of this "
+                                       "workload (committed profile)"},
         "cpu_baseline": cpu,
         "e2e": {"value": round(per * world / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
                 "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d * world,
@@ -649,6 +651,21 @@ def run_topk(args, rank, world, local):
 
 
 TOPK_METRIC = "DSA top-k page-table transform: algorithmic HBM GB/s and us/call"
+
+
+def profiled_topk_traffic(workload: str) -> int | None:
+    """DRAM read + write bytes of one launch of the top-k kernel on
+    ``workload``, from the committed ncu summary of that workload (the
+    ``traffic_bytes_per_launch`` line of a ``profiles/dsa_topk_kernel_*``
+    file whose ``workload:`` line names it)."""
+    for f in sorted((ROOT / "profiles").glob("dsa_topk_kernel_*.md")):
+        text = f.read_text()
+        if not re.search(rf"^workload: {re.escape(workload)}\b", text, flags=re.M):
+            continue
+        m = re.search(r"traffic_bytes_per_launch:\s*([0-9]+)", text)
+        if m:
+            return int(m.group(1))
+    return None
 
 
 def topk_line_config(w, world):

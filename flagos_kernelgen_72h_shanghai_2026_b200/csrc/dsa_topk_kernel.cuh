@@ -25,7 +25,7 @@
 //     the row max `hi` and t0. When t0 is above the raw key of -inf, every key >= t0 is
 //     selectable and K of them exist; otherwise (short or -inf-heavy rows)
 //     the keys are made exact and all selectable keys are candidates.
-//  3. compaction: the keys >= t0 (about 380 of 4096 at K = 128 for Gaussian
+//  3. compaction: the keys >= t0 (about 420 of 4096 at K = 128 for Gaussian
 //     scores) are appended to a shared candidate list as 64-bit codes
 //     (key << 32 | ~id), one shared atomic per warp. Codes are unique, so
 //     their order is the exact output order. If more than `cap` keys pass
