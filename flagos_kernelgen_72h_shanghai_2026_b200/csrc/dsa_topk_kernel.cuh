@@ -515,14 +515,28 @@ __global__ void __launch_bounds__(NT, NT == 128 ? 5 : NT == 256 ? 2 : 1)
           const Tin* sv = reinterpret_cast<const Tin*>(stage) + 4 * t;
           const uint32_t nid = 0xffffffffu - 4u * (uint32_t)t;  // ~id of this thread's block 0
           auto append = [&](auto fold) {
+            // two candidates per trip: independent loads and stores overlap
             while (mask) {
-              const int i = __ffs(mask) - 1;
+              const int i0 = __ffs(mask) - 1;
               mask &= mask - 1;
-              const int off = (i >> 2) * (4 * T) + (i & 3);  // id - 4t
-              uint32_t k = raw_key(to_float(sv[off]));
-              if (decltype(fold)::value) k = fold_zero(k);
-              cand[o++] = ((uint64_t)k << 32) | (uint64_t)(nid - (uint32_t)off);
-              atomicAdd(&hist[(k - lo) >> s], 1u);
+              const bool two = mask != 0;
+              const int i1 = two ? __ffs(mask) - 1 : i0;
+              mask &= two ? mask - 1 : mask;
+              const int off0 = (i0 >> 2) * (4 * T) + (i0 & 3);  // id - 4t
+              const int off1 = (i1 >> 2) * (4 * T) + (i1 & 3);
+              uint32_t k0 = raw_key(to_float(sv[off0]));
+              uint32_t k1 = raw_key(to_float(sv[off1]));
+              if (decltype(fold)::value) {
+                k0 = fold_zero(k0);
+                k1 = fold_zero(k1);
+              }
+              cand[o] = ((uint64_t)k0 << 32) | (uint64_t)(nid - (uint32_t)off0);
+              atomicAdd(&hist[(k0 - lo) >> s], 1u);
+              if (two) {
+                cand[o + 1] = ((uint64_t)k1 << 32) | (uint64_t)(nid - (uint32_t)off1);
+                atomicAdd(&hist[(k1 - lo) >> s], 1u);
+              }
+              o += two ? 2 : 1;
             }
           };
           if (lo <= kPosZero)
