@@ -100,22 +100,19 @@ __device__ __forceinline__ uint32_t fast_div(uint32_t n, uint32_t mul, uint32_t 
   return (__umulhi(n, mul) + n) >> shift;
 }
 
-// Shared-memory carve-up (dynamic part), identical on host and device: two
-// staging buffers for the scores of a row (the current row and the one in
-// flight), the candidate list, histogram and suffix counts. The
-// bin-ordered copy of the candidates (`ord`) reuses the current row's
-// staging buffer once the candidates are compacted (cap codes must fit).
+// Shared-memory carve-up (dynamic part), identical on host and device: the
+// staging buffer for a row's scores, the candidate list and its bin-ordered
+// copy, histogram and suffix counts.
 struct Smem {
-  size_t stage, stage_bytes, cand, hist, F, total;
+  size_t stage, cand, ord, hist, F, total;
 };
 __host__ __device__ inline size_t align16(size_t v) { return (v + 15) / 16 * 16; }
 __host__ __device__ inline Smem smem_layout(int T, int J, int vec_bytes, int K, int cap) {
   Smem L;
   L.stage = 0;
-  L.stage_bytes = align16((size_t)T * J * vec_bytes);
-  if (L.stage_bytes < (size_t)cap * sizeof(uint64_t)) L.stage_bytes = (size_t)cap * sizeof(uint64_t);
-  L.cand = 2 * L.stage_bytes;
-  L.hist = L.cand + (size_t)cap * sizeof(uint64_t);
+  L.cand = align16((size_t)T * J * vec_bytes);
+  L.ord = L.cand + (size_t)cap * sizeof(uint64_t);
+  L.hist = L.ord + (size_t)cap * sizeof(uint64_t);
   L.F = L.hist + align16((kBins + 1) * sizeof(uint32_t));
   L.total = L.F + align16((kBins + 1) * sizeof(uint32_t));
   return L;
@@ -312,9 +309,9 @@ __device__ __forceinline__ void write_out(const Params& p, int64_t row, uint32_t
 
 // --------------------------------------------------------------- kernel
 // NT threads per CTA (128, 256 or 512), J vectors per thread. The register
-// budget leaves room for 5 CTAs of 128 threads per SM (2 of 256).
+// budget leaves room for 6 CTAs of 128 threads per SM (2 of 256).
 template <typename Tin, int J, int NT>
-__global__ void __launch_bounds__(NT, NT == 128 ? 5 : NT == 256 ? 2 : 1)
+__global__ void __launch_bounds__(NT, NT == 128 ? 6 : NT == 256 ? 2 : 1)
     dsa_topk_kernel(const Params p) {
   using V = Vec4<Tin>;
   using raw = typename V::raw;
@@ -339,12 +336,11 @@ __global__ void __launch_bounds__(NT, NT == 128 ? 5 : NT == 256 ? 2 : 1)
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-  auto stage_buf = [&](int parity) {
-    return reinterpret_cast<raw*>(smem + L.stage + (size_t)parity * L.stage_bytes);
-  };
-  auto issue = [&](int64_t r, int n, int parity) {
+  raw* const stage = reinterpret_cast<raw*>(smem + L.stage);
+  uint64_t* const ord = reinterpret_cast<uint64_t*>(smem + L.ord);
+  auto issue = [&](int64_t r, int n) {
     const Tin* base = scores + r * (int64_t)NB + 4 * t;
-    raw* st = stage_buf(parity) + t;
+    raw* st = stage + t;
     const int nv = (n + 3) >> 2;  // vectors holding candidates (nv <= nvec)
 #pragma unroll
     for (int j = 0; j < J; ++j)
@@ -357,16 +353,22 @@ __global__ void __launch_bounds__(NT, NT == 128 ? 5 : NT == 256 ? 2 : 1)
   int n_cur = 0, n_next = 0;
   if (row < p.rows) {
     n_cur = row_candidates(p, (uint32_t)row);
-    issue(row, n_cur, 0);
+    issue(row, n_cur);
     if (row + G < p.rows) n_next = row_candidates(p, (uint32_t)(row + G));
   }
-  int rb = 0;  // parity: reduction buffer and staging buffer of this row
+  int rb = 0;  // parity of the reduction buffer
+  // The next row's copies go into the staging buffer once this row is done
+  // with it: after the compaction (every thread has passed its barrier).
+  auto issue_next = [&]() {
+    if (row + G < p.rows) {
+      issue(row + G, n_next);
+      n_cur = n_next;
+      if (row + 2 * G < p.rows) n_next = row_candidates(p, (uint32_t)(row + 2 * G));
+    }
+  };
 
   for (; row < p.rows; row += G, rb ^= 1) {
     const int n = n_cur;
-    const raw* stage = stage_buf(rb);
-    // bin-ordered candidates, in this row's staging buffer once it is consumed
-    uint64_t* ord = reinterpret_cast<uint64_t*>(smem + L.stage + (size_t)rb * L.stage_bytes);
     // ---- 1. raw keys of this row (own staged vectors), 0 when masked
     cp_async_wait_all();
     uint32_t key[J][4];
@@ -418,14 +420,6 @@ __global__ void __launch_bounds__(NT, NT == 128 ? 5 : NT == 256 ? 2 : 1)
     if (t == 0) s_C = 0;
     for (int i = t; i < kBins + 1; i += T) hist[i] = 0;
     __syncthreads();
-    // The next row's copies go to the other staging buffer. It last held the
-    // previous row's scores and bin-ordered candidates, which every thread
-    // has finished reading: all of them have passed the barrier above.
-    if (row + G < p.rows) {
-      issue(row + G, n_next, rb ^ 1);
-      n_cur = n_next;
-      if (row + 2 * G < p.rows) n_next = row_candidates(p, (uint32_t)(row + 2 * G));
-    }
     uint32_t hi = 0, lo = 0xffffffffu;
     for (int w = 0; w < nw; ++w) {
       hi = max(hi, s_red[rb][1][w]);
@@ -646,6 +640,7 @@ __global__ void __launch_bounds__(NT, NT == 128 ? 5 : NT == 256 ? 2 : 1)
         C = s_C;
       }
 
+      issue_next();
       // ---- 4. exact order of the top `need` candidates (their digit
       // histogram was counted during the compaction)
       if (warp == 0) suffix_scan_warp(hist, 0u, need, F, &s_bin);
@@ -670,6 +665,7 @@ __global__ void __launch_bounds__(NT, NT == 128 ? 5 : NT == 256 ? 2 : 1)
         if (slot < need) write_out(p, row, slot, (int32_t)(0xffffffffu - (uint32_t)code));
       }
     }
+    if (need == 0) issue_next();
     // slots beyond the selectable count
     for (int k = (int)need + t; k < K; k += T) write_out(p, row, (uint32_t)k, -1);
   }
