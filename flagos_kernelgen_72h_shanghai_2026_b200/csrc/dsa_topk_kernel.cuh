@@ -309,9 +309,10 @@ __device__ __forceinline__ void write_out(const Params& p, int64_t row, uint32_t
 
 // --------------------------------------------------------------- kernel
 // NT threads per CTA (128, 256 or 512), J vectors per thread. The register
-// budget leaves room for 6 CTAs of 128 threads per SM (2 of 256).
+// budget leaves room for 7 CTAs of 128 threads per SM (6 when J >= 7,
+// 2 of 256 threads).
 template <typename Tin, int J, int NT>
-__global__ void __launch_bounds__(NT, NT == 128 ? 6 : NT == 256 ? 2 : 1)
+__global__ void __launch_bounds__(NT, NT == 128 ? (J >= 7 ? 6 : 7) : NT == 256 ? 2 : 1)
     dsa_topk_kernel(const Params p) {
   using V = Vec4<Tin>;
   using raw = typename V::raw;
