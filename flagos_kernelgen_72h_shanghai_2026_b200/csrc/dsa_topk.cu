@@ -78,21 +78,18 @@ void pick_shape(int64_t NB, int* T, int* J) {
   *J = (int)((nvec + *T - 1) / *T);
 }
 
-// Lower-bound groups: a thread vouches for two keys (its two largest vector
-// maxima) when it holds at least two vectors, else for one (its max); a
-// group of g threads vouches for as many. g = the largest power of two <= 32
-// that leaves vouch * T / g >= K (group 0 when even g = 1 falls short: no
-// bound). A thread whose vectors are masked vouches for keys 0, which turns
-// the bound off for that row (the kernel then takes every selectable key).
-void pick_group(int T, int J, int K, int* group, int* vouch) {
-  *vouch = J >= 2 ? 2 : 1;
-  if (K > *vouch * T) {
-    *group = 0;
-    return;
-  }
+// Lower-bound groups: a thread vouches for its vouch_of(J) largest vector
+// maxima (4, 2 or 1 distinct keys), and so does a group of g threads (the
+// merged lists). g = the largest power of two <= 32 that leaves
+// vouch * T / g >= K (group 0 when even g = 1 falls short: no bound). A
+// thread whose vectors are masked vouches for keys 0, which turns the bound
+// off for that row (the kernel then takes every selectable key).
+int pick_group(int T, int J, int K) {
+  const int vouch = vouch_of(J);
+  if (K > vouch * T) return 0;
   int g = 1;
-  while (g < 32 && *vouch * T / (2 * g) >= K) g *= 2;
-  *group = g;
+  while (g < 32 && vouch * T / (2 * g) >= K) g *= 2;
+  return g;
 }
 
 int validate(const dsa_topk_args_t* a) {
@@ -206,7 +203,7 @@ int dsa_topk_launch(const dsa_topk_args_t* a, void* stream) {
   p.page_bytes = pb;
   p.blocks_bytes = bb;
   p.cap = cap;
-  pick_group(T, J, a->top_k, &p.group, &p.vouch);
+  p.group = pick_group(T, J, a->top_k);
   fast_div_init((uint32_t)p.HQ, &p.hq_mul, &p.hq_shift);
   fast_div_init((uint32_t)p.Q, &p.q_mul, &p.q_shift);
 

@@ -18,14 +18,14 @@
 // Per row, exactly:
 //  1. keys: every score becomes an order-preserving 32-bit key (a raw key
 //     first: the sign handling only), 0 for a masked block; per-thread max.
-//  2. lower bound: every thread keeps its two largest vector maxima, so it
-//     holds two distinct keys >= the second one; threads are grouped so that
-//     the groups vouch for at least K keys (two each), and the smallest
-//     group bound t0 has at least K keys >= it. One block reduction gives
+//  2. lower bound: every thread keeps its four (or two) largest vector
+//     maxima, so it holds that many distinct keys >= the last one; threads
+//     are grouped (lists merged by shuffles) so that the groups vouch for at
+//     least K keys, and the smallest group bound t0 has at least K keys >= it. One block reduction gives
 //     the row max `hi` and t0. When t0 is above the raw key of -inf, every key >= t0 is
 //     selectable and K of them exist; otherwise (short or -inf-heavy rows)
 //     the keys are made exact and all selectable keys are candidates.
-//  3. compaction: the keys >= t0 (about 420 of 4096 at K = 128 for Gaussian
+//  3. compaction: the keys >= t0 (about 300 of 4096 at K = 128 for Gaussian
 //     scores) are appended to a shared candidate list as 64-bit codes
 //     (key << 32 | ~id), one shared atomic per warp. Codes are unique, so
 //     their order is the exact output order. If more than `cap` keys pass
@@ -79,9 +79,8 @@ struct Params {
   int32_t page_bytes;    // page_table / out_pages element size (4 or 8)
   int32_t blocks_bytes;  // out_blocks element size (4 or 8)
   int32_t cap;           // candidate list capacity (>= K)
-  int32_t group;         // threads per lower-bound group (power of two <= 32), 0 = no bound
-  int32_t vouch;         // keys each group vouches for (1: its max, 2: its second largest
-                         // vector max); T / group * vouch >= K
+  int32_t group;         // threads per lower-bound group (power of two <= 32), 0 = no bound;
+                         // T / group * vouch_of(J) >= K
   uint32_t hq_mul, hq_shift;  // row / (H*Q) = fast_div(row, ...)  (rows < 2^31)
   uint32_t q_mul, q_shift;    // row / Q
 };
@@ -117,6 +116,9 @@ __host__ __device__ inline Smem smem_layout(int T, int J, int vec_bytes, int K, 
   L.total = L.F + align16((kBins + 1) * sizeof(uint32_t));
   return L;
 }
+// Keys a thread (and a group of threads) vouches for in the lower bound:
+// its 4, 2 or 1 largest vector maxima, as its J vectors allow.
+__host__ __device__ constexpr int vouch_of(int J) { return J >= 4 ? 4 : J >= 2 ? 2 : 1; }
 __host__ __device__ inline int candidate_cap(int K) { return K > kMinCap ? K : kMinCap; }
 
 // ------------------------------------------------------------------ loads
@@ -318,6 +320,8 @@ __global__ void __launch_bounds__(NT, NT == 128 ? (J >= 7 ? 6 : 7) : NT == 256 ?
   using raw = typename V::raw;
   extern __shared__ __align__(16) uint8_t smem[];
   constexpr int T = NT;
+  // keys a thread vouches for in the lower bound: its VOUCH largest vector maxima
+  constexpr int VOUCH = vouch_of(J);
   const int t = threadIdx.x;
   const int lane = t & 31, warp = t >> 5, nw = T >> 5;
   const int NB = p.NB;
@@ -373,7 +377,10 @@ __global__ void __launch_bounds__(NT, NT == 128 ? (J >= 7 ? 6 : 7) : NT == 256 ?
     // ---- 1. raw keys of this row (own staged vectors), 0 when masked
     cp_async_wait_all();
     uint32_t key[J][4];
-    uint32_t mx = 0, mx2 = 0;  // largest and second largest of the vector maxima
+    // the VOUCH largest vector maxima of this thread, descending (a[0] = max)
+    uint32_t a[VOUCH];
+#pragma unroll
+    for (int i = 0; i < VOUCH; ++i) a[i] = 0;
     {
       const int nfv = n >> 2;  // vectors whose four blocks are all candidates
 #pragma unroll
@@ -390,24 +397,41 @@ __global__ void __launch_bounds__(NT, NT == 128 ? (J >= 7 ? 6 : 7) : NT == 256 ?
 #pragma unroll
           for (int c = 0; c < 4; ++c) key[j][c] = 4 * v + c < n ? raw_key(f[c]) : 0u;
         }
-        const uint32_t vm = max(max(key[j][0], key[j][1]), max(key[j][2], key[j][3]));
-        mx2 = max(mx2, min(mx, vm));
-        mx = max(mx, vm);
+        uint32_t vm = max(max(key[j][0], key[j][1]), max(key[j][2], key[j][3]));
+#pragma unroll
+        for (int i = 0; i < VOUCH; ++i) {  // insert into the sorted list
+          const uint32_t hi_i = max(a[i], vm);
+          vm = min(a[i], vm);
+          a[i] = hi_i;
+        }
       }
     }
     // ---- 2. block reduction: max raw key and the lower bound t0. A thread
-    // holds at least two keys >= mx2 (the maxima of two vectors); a group of
-    // threads at least two keys >= the second largest of its members' (mx,
-    // mx2) pairs. With T / group * 2 >= K groups' worth of distinct keys, at
-    // least K keys are >= t0 = the smallest group's second largest.
-    uint32_t g1 = mx, g2 = mx2;
+    // holds VOUCH distinct keys >= a[VOUCH-1] (the maxima of VOUCH of its
+    // vectors); a group of threads holds VOUCH distinct keys >= the VOUCH-th
+    // largest of its members' lists (merged by xor shuffles). With
+    // T / group * VOUCH >= K, at least K keys are >= t0 = the smallest
+    // group's VOUCH-th largest.
+    const uint32_t mx = a[0];
     for (int o = 1; o < p.group; o <<= 1) {
-      const uint32_t b1 = __shfl_xor_sync(0xffffffffu, g1, o);
-      const uint32_t b2 = __shfl_xor_sync(0xffffffffu, g2, o);
-      g2 = max(min(g1, b1), max(g2, b2));
-      g1 = max(g1, b1);
+      uint32_t b[VOUCH];
+#pragma unroll
+      for (int i = 0; i < VOUCH; ++i) b[i] = __shfl_xor_sync(0xffffffffu, a[i], o);
+      // top VOUCH of two descending lists: pairwise max against the reversed
+      // partner list gives them as a bitonic sequence, then sort it
+#pragma unroll
+      for (int i = 0; i < VOUCH; ++i) a[i] = max(a[i], b[VOUCH - 1 - i]);
+#pragma unroll
+      for (int w = VOUCH / 2; w > 0; w /= 2)
+#pragma unroll
+        for (int i = 0; i < VOUCH; ++i)
+          if ((i & w) == 0) {
+            const uint32_t x = a[i], y = a[i + w];
+            a[i] = max(x, y);
+            a[i + w] = min(x, y);
+          }
     }
-    uint32_t t0 = p.group > 0 ? (p.vouch == 2 ? g2 : g1) : 0u;
+    uint32_t t0 = p.group > 0 ? a[VOUCH - 1] : 0u;
     uint32_t wmx = mx;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
