@@ -786,8 +786,9 @@ def run_pcie(args, rank, world, local):
 def run_latency(args, local):
     """Small-M latency regime (M <= 128, where the reference's launch
     overhead dominates): host microseconds per eager call (the Python
-    wrapper, argument struct and launch; measured on the host clock over
-    calls issued back to back), device microseconds per call (CUDA events,
+    wrapper and its C++ launch path; beside it the ctypes path with and
+    without its argument-struct cache; host clock over calls issued back to
+    back), device microseconds per call (CUDA events,
     eager), and device microseconds per call when the calls are replayed from
     one CUDA graph. Prints its own JSON line; not the default benchmark."""
     from flagos_kernelgen_72h_shanghai_2026_b200 import fused_add_rmsnorm_group_quant
@@ -814,15 +815,27 @@ def run_latency(args, local):
             call()
         host_us = (time.perf_counter() - t0) / n * 1e6
         torch.cuda.synchronize(dev)
-        # the same calls with the argument-struct cache emptied before each
-        # one: the full Python-side checks and struct fill every time
+        # the ctypes path (the C++ launch path switched off): with the
+        # argument-struct cache, and with it emptied before every call
         from flagos_kernelgen_72h_shanghai_2026_b200 import task01
-        t0 = time.perf_counter()
-        for _ in range(n):
-            task01._tls.args = {}
-            call()
-        host_us_nocache = (time.perf_counter() - t0) / n * 1e6
-        torch.cuda.synchronize(dev)
+        fast, task01._fast = task01._fast, None
+        try:
+            for _ in range(50):
+                call()
+            torch.cuda.synchronize(dev)
+            t0 = time.perf_counter()
+            for _ in range(n):
+                call()
+            host_us_ctypes = (time.perf_counter() - t0) / n * 1e6
+            torch.cuda.synchronize(dev)
+            t0 = time.perf_counter()
+            for _ in range(n):
+                task01._tls.args = {}
+                call()
+            host_us_nocache = (time.perf_counter() - t0) / n * 1e6
+            torch.cuda.synchronize(dev)
+        finally:
+            task01._fast = fast
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
@@ -850,7 +863,8 @@ def run_latency(args, local):
         torch.cuda.synchronize(dev)
         graph_us = e0.elapsed_time(e1) / 2000 * 1e3
         res[f"M{M}"] = {"host_us_per_call": round(host_us, 2),
-                        "host_us_per_call_uncached": round(host_us_nocache, 2),
+                        "host_us_per_call_ctypes_cached": round(host_us_ctypes, 2),
+                        "host_us_per_call_ctypes_uncached": round(host_us_nocache, 2),
                         "device_us_per_call_eager": round(eager_us, 2),
                         "device_us_per_call_graph": round(graph_us, 2)}
     print(json.dumps({"metric": "small-M latency, us/call (D = 7168, bf16 -> e4m3)",

@@ -13,6 +13,7 @@ libdsa_topk.so (C ABI: include/dsa_topk.h).
 from .offload import fused_add_rmsnorm_group_quant_host  # noqa: F401
 from .task01 import fused_add_rmsnorm_group_quant, launch_plan  # noqa: F401
 from .task02 import dsa_topk_page_table_transform  # noqa: F401
+from . import task01, task02  # noqa: F401,E402
 
 __all__ = ["fused_add_rmsnorm_group_quant", "fused_add_rmsnorm_group_quant_host", "launch_plan",
            "dsa_topk_page_table_transform"]

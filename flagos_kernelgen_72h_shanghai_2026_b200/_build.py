@@ -77,8 +77,47 @@ def build_topk_lib(force: bool = False, verbose: bool = False) -> Path:
     return _compile(TOPK_SOURCES, TOPK_LIB_PATH, verbose)
 
 
+FAST_SOURCE = CSRC_DIR / "farq_fast.cpp"
+
+
+def fast_ext_path() -> Path:
+    import sysconfig
+    return PKG_DIR / ("_farq_fast" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_fast_ext(force: bool = False, verbose: bool = False) -> Path:
+    """Compile the C++ launch path of the Python operators (_farq_fast, a
+    torch extension module linked against libfarq.so and libdsa_topk.so)
+    with g++, in-tree, if it is missing or older than its sources."""
+    out = fast_ext_path()
+    deps = [FAST_SOURCE, INCLUDE_DIR / "farq.h", INCLUDE_DIR / "dsa_topk.h", LIB_PATH, TOPK_LIB_PATH]
+    if not force and not _stale(out, deps):
+        return out
+    import sysconfig
+
+    import torch
+    from torch.utils import cpp_extension
+
+    cuda_home = os.path.dirname(os.path.dirname(_nvcc()))
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    cmd = ["g++", "-O2", "-std=c++17", "-shared", "-fPIC", "-w",
+           f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_EXTENSION_NAME=_farq_fast",
+           "-DTORCH_API_INCLUDE_EXTENSION_H",
+           *[f"-I{p}" for p in cpp_extension.include_paths()],
+           f"-I{sysconfig.get_paths()['include']}", f"-I{cuda_home}/include", f"-I{INCLUDE_DIR}",
+           str(FAST_SOURCE), "-o", str(out) + ".tmp",
+           *[f"-L{p}" for p in cpp_extension.library_paths()],
+           "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-ltorch_python",
+           f"-L{PKG_DIR}", "-lfarq", "-ldsa_topk",
+           "-Wl,-rpath,$ORIGIN", *[f"-Wl,-rpath,{p}" for p in cpp_extension.library_paths()]]
+    _run(cmd, verbose)
+    os.replace(str(out) + ".tmp", out)
+    return out
+
+
 def build_all(force: bool = False, verbose: bool = False) -> list[Path]:
-    return [build_lib(force, verbose), build_topk_lib(force, verbose)]
+    libs = [build_lib(force, verbose), build_topk_lib(force, verbose)]
+    return libs + [build_fast_ext(force, verbose)]
 
 
 def _compile(sources: list[Path], lib_path: Path, verbose: bool) -> Path:

@@ -32,6 +32,12 @@ import torch
 
 from . import _lib
 
+try:  # C++ launch path (csrc/farq_fast.cpp); without it every call takes the ctypes path
+    from . import _farq_fast as _fast
+except ImportError:
+    _fast = None
+_T = torch.Tensor
+
 _IN_DTYPES = {torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_FP16}
 _FLOAT_DTYPES = {
     torch.bfloat16: _lib.DTYPE_BF16,
@@ -78,6 +84,15 @@ def _meta(t):
     return (t.device, t.shape, t.stride(), t.dtype)
 
 
+def _raise_status(st: int):
+    msg = f"farq_launch failed: {_lib.strerror(st)} (status {st})"
+    if st in _VALUE_ERRORS:
+        raise ValueError(msg)
+    if st == _lib.ERR_BAD_DTYPE:
+        raise TypeError(msg)
+    raise RuntimeError(msg)
+
+
 def _launch(a, device):
     lib = _lib.load()
     if torch.cuda.current_device() != device.index:
@@ -86,12 +101,7 @@ def _launch(a, device):
     else:
         st = lib.farq_launch(ctypes.byref(a), torch.cuda.current_stream(device).cuda_stream)
     if st != _lib.OK:
-        msg = f"farq_launch failed: {_lib.strerror(st)} (status {st})"
-        if st in _VALUE_ERRORS:
-            raise ValueError(msg)
-        if st == _lib.ERR_BAD_DTYPE:
-            raise TypeError(msg)
-        raise RuntimeError(msg)
+        _raise_status(st)
 
 
 def fused_add_rmsnorm_group_quant(
@@ -116,6 +126,22 @@ def fused_add_rmsnorm_group_quant(
     """residual_out = x + residual; norm = RMSNorm(residual_out) * gamma;
     per-group quantisation of norm into (x_q, x_scale). Asynchronous on the
     current CUDA stream; returns (residual_out, norm_out, x_q, x_scale)."""
+    # C++ launch path for the common case (contiguous tensors on one device,
+    # no test or tuning options); -1 = not handled, continue below.
+    if (_fast is not None and _T is type(x) and _T is type(residual) and _T is type(gamma)
+            and _T is type(residual_out) and _T is type(x_q) and _T is type(x_scale)
+            and (norm_out is None or _T is type(norm_out)) and _status is None
+            and not (_test_force_timeout or _tune_ctas_per_sm or _tune_teams_per_cta
+                     or _tune_stages or _tune_vec_per_thread)):
+        try:
+            st = _fast.task01(x, residual, gamma, residual_out, norm_out, x_q, x_scale, eps,
+                              group_size, bool(ue8m0))
+        except TypeError:  # a scalar pybind11 cannot convert: the checks below report it
+            st = -1
+        if st == _lib.OK:
+            return residual_out, norm_out, x_q, x_scale
+        if st > 0:
+            _raise_status(st)
     key = None
     if (isinstance(x, torch.Tensor) and isinstance(residual, torch.Tensor)
             and isinstance(gamma, torch.Tensor) and isinstance(residual_out, torch.Tensor)

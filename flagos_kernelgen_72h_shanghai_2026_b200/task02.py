@@ -28,6 +28,12 @@ import torch
 
 from . import _topk_lib as L
 
+try:  # C++ launch path (csrc/farq_fast.cpp); without it every call takes the ctypes path
+    from . import _farq_fast as _fast
+except ImportError:
+    _fast = None
+_T = torch.Tensor
+
 _SCORE_DTYPES = {torch.float32: L.DTYPE_FP32, torch.bfloat16: L.DTYPE_BF16,
                  torch.float16: L.DTYPE_FP16}
 _INDEX_DTYPES = {torch.int32: L.DTYPE_INT32, torch.int64: L.DTYPE_INT64}
@@ -69,6 +75,17 @@ def dsa_topk_page_table_transform(scores: torch.Tensor, page_table: torch.Tensor
     kv_lens [B]; out_blocks, out_pages [B, H, Q, top_k] (int32 or int64;
     out_pages has page_table's dtype). The launch is asynchronous on the
     current CUDA stream."""
+    if (_fast is not None and _T is type(scores) and _T is type(page_table) and _T is type(q_pos)
+            and _T is type(kv_lens) and _T is type(out_blocks) and _T is type(out_pages)):
+        try:
+            st = _fast.task02(scores, page_table, q_pos, kv_lens, out_blocks, out_pages,
+                              block_size, top_k)
+        except TypeError:  # a scalar pybind11 cannot convert: the checks below report it
+            st = -1
+        if st == L.OK:
+            return out_blocks, out_pages
+        if st > 0:
+            _raise_status(st)
     dev = _tensor("scores", scores, None)
     for n, t in (("page_table", page_table), ("q_pos", q_pos), ("kv_lens", kv_lens),
                  ("out_blocks", out_blocks), ("out_pages", out_pages)):
@@ -113,10 +130,14 @@ def dsa_topk_page_table_transform(scores: torch.Tensor, page_table: torch.Tensor
         stream = torch.cuda.current_stream(dev).cuda_stream
         st = L.load().dsa_topk_launch(ctypes.byref(a), ctypes.c_void_p(stream))
     if st != L.OK:
-        msg = f"dsa_topk_page_table_transform: {L.strerror(st)}"
-        if st in _VALUE_ERRORS:
-            raise ValueError(msg)
-        if st == L.ERR_BAD_DTYPE:
-            raise TypeError(msg)
-        raise RuntimeError(msg)
+        _raise_status(st)
     return out_blocks, out_pages
+
+
+def _raise_status(st: int):
+    msg = f"dsa_topk_page_table_transform: {L.strerror(st)}"
+    if st in _VALUE_ERRORS:
+        raise ValueError(msg)
+    if st == L.ERR_BAD_DTYPE:
+        raise TypeError(msg)
+    raise RuntimeError(msg)
