@@ -336,6 +336,10 @@ def run_ours(args, w, rank, world, local):
     # ---- end to end: pinned host inputs -> device -> operator -> host outputs
     e2e = run_e2e(args, w, rows, dev, g, start, rank, pg)
 
+    # ---- N > 1: the tensor-parallel variant (all-reduce fused with the
+    # operator) at the DeepSeek-V3 shape, checked and timed on every rank
+    tp = tp_leg(rank, world, dev, pg) if (world > 1 and not args.no_tp) else None
+
     times = torch.tensor([total_ms, kern_ms, iso_ms, e2e["ms"],
                           dsv3["us_per_call"] if dsv3 else 0.0], dtype=torch.float64, device=dev)
     if pg:
@@ -394,6 +398,7 @@ def run_ours(args, w, rank, world, local):
                      "traffic_source": "ncu per-row DRAM bytes of a smaller capture x rows per "
                                        "launch" if traffic_row else None},
         "dsv3_4096x7168_per_gpu": dsv3,
+        "tp_allreduce_fused_4096x7168": tp,
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_gbs, 3), "unit": "GB/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": e2e["h2d"] * world, "d2h_bytes_per_step": e2e["d2h"] * world,
@@ -406,6 +411,85 @@ def run_ours(args, w, rank, world, local):
                    "window": "warm-up and timed region (sampler started before the warm-up)"},
     }
     print(json.dumps(line), flush=True)
+
+
+def tp_leg(rank, world, dev, pg, steps: int = 100, warmup: int = 20) -> dict:
+    """Tensor-parallel variant (tp.TPFusedNormQuant, farq_ar_launch) on all N
+    ranks at 4096 x 7168: x = bf16(sum of the N ranks' partials) fused with
+    the operator, every output row replicated to every rank. Checked on every
+    rank against the single-GPU kernel applied to the same x (computed
+    locally from the seeded partials: residual_out bit-exact, scales within
+    1e-6 relative, q within one e4m3 step on at most 0.1 % of elements), then
+    timed against NCCL all-reduce + the single-GPU kernel (device time, max
+    over ranks). Runs after the main timing; not part of `value`."""
+    import torch.distributed as dist
+    from flagos_kernelgen_72h_shanghai_2026_b200 import fused_add_rmsnorm_group_quant
+    from flagos_kernelgen_72h_shanghai_2026_b200.tp import TPFusedNormQuant
+
+    w = CONFIGS[2]
+    M, D, G = w.M, w.D, w.group_size
+    op = TPFusedNormQuant(M, D, G, dtype=w.dtype, q_dtype=w.q_dtype)
+
+    def partial(k):
+        gen = torch.Generator().manual_seed(7000 + k)
+        return torch.randn(M, D, generator=gen).to(w.dtype)
+
+    gen = torch.Generator().manual_seed(6999)
+    residual = (2 * torch.randn(M, D, generator=gen)).to(w.dtype).to(dev)
+    gamma = (1 + 0.1 * torch.randn(D, generator=gen)).to(w.dtype).to(dev)
+    mine = partial(rank).to(dev)
+    op.partial_buffer(M).copy_(mine)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    ro, _, q, s = op(M, residual, gamma, w.eps, status=status)
+    torch.cuda.synchronize(dev)
+    # reference on this GPU: x in rank order, summed in fp32, rounded once
+    x = torch.zeros(M, D, dtype=torch.float32, device=dev)
+    for k in range(world):
+        x += (mine if k == rank else partial(k).to(dev)).float()
+    x = x.to(w.dtype)
+    rro, rno, rq, rs = alloc_outputs(w, M, dev)
+    fused_add_rmsnorm_group_quant(x, residual, gamma, rro, rno, rq, rs, w.eps, G)
+    torch.cuda.synchronize(dev)
+    ok = int(status.item()) == 0 and torch.equal(ro.view(torch.int16), rro.view(torch.int16))
+    ok = ok and float(((s - rs).abs() / rs.abs()).max()) <= 1e-6
+
+    def ordered(b):
+        b = b.view(torch.uint8).to(torch.int32)
+        return torch.where(b >= 128, -(b & 127), b)
+
+    dq = (ordered(q) - ordered(rq)).abs()
+    ok = ok and int(dq.max()) <= 1 and float((dq != 0).float().mean()) <= 1e-3
+    del x, rno
+    xr = torch.empty_like(mine)
+
+    def fused():
+        op(M, residual, gamma, w.eps)
+
+    def unfused():
+        xr.copy_(mine)
+        dist.all_reduce(xr)
+        fused_add_rmsnorm_group_quant(xr, residual, gamma, rro, None, rq, rs, w.eps, G)
+
+    res = []
+    for f in (fused, unfused):
+        for _ in range(warmup):
+            f()
+        torch.cuda.synchronize(dev)
+        pg.barrier()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(steps):
+            f()
+        t1.record()
+        torch.cuda.synchronize(dev)
+        res.append(t0.elapsed_time(t1) / steps * 1e3)
+    out = torch.tensor(res + [0.0 if ok else 1.0], dtype=torch.float64, device=dev)
+    pg.all_reduce(out, op=pg.ReduceOp.MAX)
+    return {"world": world, "M": M, "D": D, "fused_us_per_call": round(float(out[0]), 2),
+            "nccl_allreduce_then_kernel_us_per_call": round(float(out[1]), 2),
+            "check_vs_single_gpu_kernel": "ok" if float(out[2]) == 0.0 else "FAILED",
+            "timing": f"{steps} calls between CUDA events after {warmup} warm-ups, max over ranks"}
 
 
 def run_e2e(args, w, rows, dev, g, start, rank, pg):
@@ -908,6 +992,8 @@ def main():
     ap.add_argument("--ref-budget", type=float, default=90.0,
                     help="seconds of CPU work for the whole --impl reference run")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-tp", action="store_true",
+                    help="N > 1: skip the tensor-parallel leg reported beside the main line")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
