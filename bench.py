@@ -333,6 +333,10 @@ def run_ours(args, w, rank, world, local):
                 "us_per_call": ms2 / k2 * 1e3, "bytes_per_call": per2}
         del sets2, step2
 
+    # ---- the next scope row: the DSA top-k page-table transform at its
+    # largest competition shape, on every GPU (per GPU, device time)
+    topk = None if args.no_topk else topk_side_leg(args, rank, dev, stream, pg)
+
     # ---- end to end: pinned host inputs -> device -> operator -> host outputs
     e2e = run_e2e(args, w, rows, dev, g, start, rank, pg)
 
@@ -341,7 +345,8 @@ def run_ours(args, w, rank, world, local):
     tp = tp_leg(rank, world, dev, pg) if (world > 1 and not args.no_tp) else None
 
     times = torch.tensor([total_ms, kern_ms, iso_ms, e2e["ms"],
-                          dsv3["us_per_call"] if dsv3 else 0.0], dtype=torch.float64, device=dev)
+                          dsv3["us_per_call"] if dsv3 else 0.0,
+                          topk["us_per_call"] if topk else 0.0], dtype=torch.float64, device=dev)
     if pg:
         pg.all_reduce(times, op=pg.ReduceOp.MAX)
         clk_all = [None] * world
@@ -362,6 +367,10 @@ def run_ours(args, w, rank, world, local):
     achieved = kernel_bytes / (kern_ms * 1e-3) / 1e9
     peak, peak_kind = load_peak()
     e2e_gbs = jb / (e2e_ms * 1e-3) / 1e9
+    if topk:
+        topk["us_per_call"] = round(float(times[5]), 2)  # max over ranks
+        topk["gbs_per_gpu"] = round(topk["bytes_per_call"] / (float(times[5]) * 1e-6) / 1e9, 2)
+        topk["frac_of_peak"] = round(topk["gbs_per_gpu"] / load_peak()[0], 4)
     if dsv3:
         dsv3["us_per_call"] = float(times[4])  # max over ranks
         dsv3["gbs_per_gpu"] = round(dsv3["bytes_per_call"] / (dsv3["us_per_call"] * 1e-6) / 1e9, 2)
@@ -399,6 +408,7 @@ def run_ours(args, w, rank, world, local):
                                        "launch" if traffic_row else None},
         "dsv3_4096x7168_per_gpu": dsv3,
         "tp_allreduce_fused_4096x7168": tp,
+        "dsa_topk_per_gpu": topk,
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_gbs, 3), "unit": "GB/s", "ms_per_step": e2e_ms,
                 "h2d_bytes_per_step": e2e["h2d"] * world, "d2h_bytes_per_step": e2e["d2h"] * world,
@@ -411,6 +421,33 @@ def run_ours(args, w, rank, world, local):
                    "window": "warm-up and timed region (sampler started before the warm-up)"},
     }
     print(json.dumps(line), flush=True)
+
+
+def topk_side_leg(args, rank, dev, stream, pg) -> dict:
+    """Task 02 (dsa_topk_page_table_transform) at its largest competition
+    shape (fp32 scores, 32768 rows x 4096 blocks, K = 128) on this GPU:
+    back-to-back launches between CUDA events after a warm-up, rotating
+    score sets over 3x L2. Reported beside the main line; `--mode topk` is
+    the full measurement of that path."""
+    from flagos_kernelgen_72h_shanghai_2026_b200 import dsa_topk_page_table_transform
+    from flagos_kernelgen_72h_shanghai_2026_b200.topk_workloads import (
+        TOPK_CONFIGS, make_topk_inputs, topk_bytes_per_call)
+
+    w = TOPK_CONFIGS["t2_nb4096_k128_2x32x512"]
+    per = topk_bytes_per_call(w)
+    nsets = 1 if per >= 3 * L2_BYTES else min(16, max(2, -(-(3 * L2_BYTES) // per)))
+    s, pt, qp, kv = make_topk_inputs(w.with_(seed=w.seed + rank), device=dev)
+    sets = [(s if i == 0 else s.roll(i, dims=2).contiguous()) for i in range(nsets)]
+    ob = torch.empty(w.B, w.H, w.Q, w.top_k, dtype=torch.int32, device=dev)
+    op = torch.empty_like(ob)
+
+    def step(i):
+        dsa_topk_page_table_transform(sets[i % nsets], pt, qp, kv, ob, op, w.block_size, w.top_k)
+
+    k = 200
+    ms, warm = timed_steps(step, k, args.warmup, stream, dev, pg, args.min_warm_s)
+    return {"workload": w.name, "steps": k, "warmup": warm, "us_per_call": ms / k * 1e3,
+            "bytes_per_call": per, "dtype": "fp32 scores, int32 ids and pages"}
 
 
 def tp_leg(rank, world, dev, pg, steps: int = 100, warmup: int = 20) -> dict:
@@ -992,6 +1029,8 @@ def main():
     ap.add_argument("--ref-budget", type=float, default=90.0,
                     help="seconds of CPU work for the whole --impl reference run")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-topk", action="store_true",
+                    help="skip the DSA top-k figure reported beside the main line")
     ap.add_argument("--no-tp", action="store_true",
                     help="N > 1: skip the tensor-parallel leg reported beside the main line")
     args = ap.parse_args()
